@@ -1,0 +1,484 @@
+// C ABI of the sparse-decode library: validation, launch-shape choice and template dispatch.
+// Declarations and contracts: include/attention_lab_b200.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+
+#include "al_decode.cuh"
+#include "al_index.cuh"
+#include "../../include/attention_lab_b200.h"
+
+namespace al {
+__device__ unsigned g_al_error;   // kernel error bits (see kErr*)
+}
+
+using namespace al;
+
+namespace {
+
+thread_local char g_msg[1024] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_msg, sizeof(g_msg), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(AL_ECUDA, "%s: %s", where, cudaGetErrorString(e));
+}
+
+struct DeviceInfo {
+  int sms = 0;
+  int max_smem_optin = 0;
+  unsigned* err = nullptr;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+std::unordered_map<unsigned long long, int> g_smem_set;   // (kernel, device) -> dynamic smem bytes allowed
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(AL_ECUDA, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.err) {
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+    if ((e = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute(max shared memory)");
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_al_error)) != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    d.err = static_cast<unsigned*>(p);
+  }
+  *out = &d;
+  return AL_OK;
+}
+
+template <typename K>
+int prepare_kernel(K kernel, size_t smem, int cs) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const unsigned long long key = (reinterpret_cast<unsigned long long>(reinterpret_cast<const void*>(kernel)) << 6) ^
+                                 (unsigned long long)dev;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_smem_set.find(key);
+  if (it == g_smem_set.end() || it->second < (int)smem) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(non-portable cluster)");
+    g_smem_set[key] = (int)smem;
+  }
+  (void)cs;
+  return AL_OK;
+}
+
+std::unordered_map<unsigned long long, int> g_cluster_ok;   // (kernel, cs, smem, device) -> schedulable
+
+template <typename K, typename P>
+int launch(K kernel, dim3 grid, int cs, size_t smem, void* stream, const P& p) {
+  int rc = prepare_kernel(kernel, smem, cs);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cs > 1) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const unsigned long long key = (reinterpret_cast<unsigned long long>(reinterpret_cast<const void*>(kernel)) << 16) ^
+                                   ((unsigned long long)cs << 40) ^ ((unsigned long long)smem << 8) ^ (unsigned long long)dev;
+    int ok = -1;
+    {
+      std::lock_guard<std::mutex> lk(g_mu);
+      auto it = g_cluster_ok.find(key);
+      if (it != g_cluster_ok.end()) ok = it->second;
+    }
+    if (ok < 0) {
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kernel, &cfg);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaOccupancyMaxActiveClusters");
+      ok = n > 0 ? 1 : 0;
+      std::lock_guard<std::mutex> lk(g_mu);
+      g_cluster_ok[key] = ok;
+    }
+    if (!ok) return fail(AL_EUNSUPPORTED, "a cluster of %d CTAs with %zu bytes of shared memory cannot be scheduled", cs, smem);
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
+  return AL_OK;
+}
+
+int plain_launch_check(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return AL_OK;
+}
+
+bool dtype_ok(int t) { return t == AL_F32 || t == AL_BF16; }
+int esize(int t) { return t == AL_F32 ? 4 : 2; }
+int pad_heads(int h) { return h <= 1 ? 1 : (h <= 2 ? 2 : 4); }
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Static shared memory of the fused kernel (upper bound used for the dynamic budget).
+constexpr int kFusedStaticBytes = 24 * 1024;
+constexpr int kAttendStaticBytes = 4 * 1024;
+
+int engine_smem(int kv_dtype, int hp) {
+  switch (kv_dtype * 8 + hp) {
+    case AL_F32 * 8 + 1: return AttendCfg<float, 1>::SMEM;
+    case AL_F32 * 8 + 2: return AttendCfg<float, 2>::SMEM;
+    case AL_F32 * 8 + 4: return AttendCfg<float, 4>::SMEM;
+    case AL_BF16 * 8 + 1: return AttendCfg<__nv_bfloat16, 1>::SMEM;
+    case AL_BF16 * 8 + 2: return AttendCfg<__nv_bfloat16, 2>::SMEM;
+    default: return AttendCfg<__nv_bfloat16, 4>::SMEM;
+  }
+}
+
+// Automatic cluster size: enough CTAs to cover the SMs, and few enough keys per CTA to fit shared memory.
+int auto_cluster(int segs, int M, int sms, int max_keys) {
+  int cs = 1;
+  while (cs < kMaxCluster && (long long)M > (long long)cs * max_keys) cs <<= 1;
+  while (cs < kMaxCluster && segs * cs < sms && M / (cs * 2) >= 256) cs <<= 1;
+  return cs;
+}
+
+template <typename KV_T, typename IDX_T>
+int dispatch_fused_h(const DecodeParams& p, int hp, dim3 grid, int cs, size_t smem, void* stream) {
+  switch (hp) {
+    case 1: return launch(sparse_step_kernel<KV_T, IDX_T, 1>, grid, cs, smem, stream, p);
+    case 2: return launch(sparse_step_kernel<KV_T, IDX_T, 2>, grid, cs, smem, stream, p);
+    default: return launch(sparse_step_kernel<KV_T, IDX_T, 4>, grid, cs, smem, stream, p);
+  }
+}
+
+int dispatch_fused(const DecodeParams& p, int kv_dtype, int idx_dtype, int hp, dim3 grid, int cs, size_t smem,
+                   void* stream) {
+  if (kv_dtype == AL_BF16 && idx_dtype == AL_F32) return dispatch_fused_h<__nv_bfloat16, float>(p, hp, grid, cs, smem, stream);
+  if (kv_dtype == AL_BF16 && idx_dtype == AL_BF16) return dispatch_fused_h<__nv_bfloat16, __nv_bfloat16>(p, hp, grid, cs, smem, stream);
+  if (kv_dtype == AL_F32 && idx_dtype == AL_F32) return dispatch_fused_h<float, float>(p, hp, grid, cs, smem, stream);
+  return dispatch_fused_h<float, __nv_bfloat16>(p, hp, grid, cs, smem, stream);
+}
+
+int dispatch_attend(const AttendParams& p, int kv_dtype, int hp, dim3 grid, int cs, size_t smem, void* stream) {
+  if (kv_dtype == AL_BF16) {
+    switch (hp) {
+      case 1: return launch(attend_kernel<__nv_bfloat16, 1>, grid, cs, smem, stream, p);
+      case 2: return launch(attend_kernel<__nv_bfloat16, 2>, grid, cs, smem, stream, p);
+      default: return launch(attend_kernel<__nv_bfloat16, 4>, grid, cs, smem, stream, p);
+    }
+  }
+  switch (hp) {
+    case 1: return launch(attend_kernel<float, 1>, grid, cs, smem, stream, p);
+    case 2: return launch(attend_kernel<float, 2>, grid, cs, smem, stream, p);
+    default: return launch(attend_kernel<float, 4>, grid, cs, smem, stream, p);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Shared validation + launch of the fused kernel (decode step or select-only).
+int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, void* stream, bool attend) {
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (!dtype_ok(idx_dtype) || (attend && !dtype_ok(kv_dtype))) return fail(AL_EINVAL, "unknown dtype code");
+  if (p.B <= 0 || p.G <= 0 || p.C <= 0) return fail(AL_EINVAL, "B, G and C must be positive");
+  if (p.B * (long long)p.G > 65535) return fail(AL_EUNSUPPORTED, "B*G = %lld exceeds 65535", p.B * (long long)p.G);
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (p.r < 1 || p.r > kMaxR) return fail(AL_EUNSUPPORTED, "index width r must be in [1, %d], got %d", kMaxR, p.r);
+  if (attend && (p.h < 1 || p.h > 4)) return fail(AL_EUNSUPPORTED, "heads per group must be in [1, 4], got %d", p.h);
+  if (!(0 <= p.lo && p.lo <= p.hi && p.hi <= p.C))
+    return fail(AL_EINVAL, "need 0 <= lo <= hi <= C, got lo=%d hi=%d C=%d", p.lo, p.hi, p.C);
+  p.M = p.hi - p.lo;
+  if (p.k < 0 || p.k > p.M) return fail(AL_EINVAL, "k=%d must lie in [0, hi-lo=%d]", p.k, p.M);
+  if (p.F < 0 || p.S != p.F + p.k)
+    return fail(AL_EINVAL, "selected_count=%d must equal fixed_count=%d + k=%d", p.S, p.F, p.k);
+  if (p.S < 1) return fail(AL_EINVAL, "at least one row must be selected");
+  if (p.k_new && (p.write_col < 0 || p.write_col >= p.C))
+    return fail(AL_EINVAL, "write_col=%d must lie in [0, C=%d)", p.write_col, p.C);
+  if (p.k_new && p.lo <= p.write_col && p.write_col < p.hi)
+    return fail(AL_EINVAL, "write_col=%d must lie outside the scanned range [%d, %d)", p.write_col, p.lo, p.hi);
+  const long long total = (long long)p.B * p.G * p.C;
+  if (total >= 0xffffffffLL) return fail(AL_EUNSUPPORTED, "B*G*C = %lld rows exceeds 2^32-1", total);
+  p.total_rows = total;
+  if (!p.zT || !p.off_lo || (p.F > 0 && !p.fixed_rows)) return fail(AL_EINVAL, "null zT, off_lo or fixed_rows");
+  if (attend && (!p.q || !p.k_cache || !p.v_cache || (!p.out && !p.part)))
+    return fail(AL_EINVAL, "null q, cache or output pointer");
+  if (attend && (!aligned16(p.k_cache) || !aligned16(p.v_cache)))
+    return fail(AL_EUNSUPPORTED, "k_cache and v_cache must start on a 16-byte boundary");
+  if (!p.u_in && p.k > 0 && p.k < p.M && (!p.q_pre || !p.wq_t)) return fail(AL_EINVAL, "null q_pre or wq_t");
+  if (p.k_new && !p.wk) return fail(AL_EINVAL, "k_pre_new given without wk");
+
+  p.select_mode = p.k == 0 ? 0 : (p.k == p.M ? 2 : 1);
+  p.scan = (p.select_mode == 1 || p.scores_out) ? 1 : 0;
+  if (p.scan && !p.u_in && (!p.q_pre || !p.wq_t)) return fail(AL_EINVAL, "null q_pre or wq_t");
+  const int ez = esize(idx_dtype);
+  p.zvec = ((long long)p.C * ez % 16 == 0) && aligned16(p.zT) ? 1 : 0;
+
+  const int hp = attend ? pad_heads(p.h) : 1;
+  const int eng = attend ? engine_smem(kv_dtype, hp) : 0;
+  const int budget = di->max_smem_optin - kFusedStaticBytes;
+  const int max_keys = (budget - 4096 - 8 * 1024) / 4;   // room left for the row list
+  int cs = cluster > 0 ? cluster : auto_cluster(p.B * p.G, p.M, di->sms, max_keys);
+  if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
+  p.cpc = (int)round_up((size_t)((p.M + cs - 1) / cs), 8);
+  if (p.cpc == 0) p.cpc = 8;
+  const size_t keys_bytes = p.scan || p.select_mode != 0 ? (size_t)p.cpc * 4 : 0;
+  p.union_bytes = (int)round_up(keys_bytes > (size_t)eng ? keys_bytes : (size_t)eng, 128);
+  const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
+  const size_t smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
+  if ((long long)smem > budget)
+    return fail(AL_EUNSUPPORTED, "candidate range too large for cluster %d: %zu bytes of shared memory per CTA", cs, smem);
+  p.err = di->err;
+  dim3 grid((unsigned)cs, (unsigned)(p.B * p.G), 1);
+  if (!attend) { p.out = nullptr; p.part = nullptr; }
+  return dispatch_fused(p, attend ? kv_dtype : AL_BF16, idx_dtype, hp, grid, cs, smem, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* al_last_error(void) { return g_msg; }
+
+int al_version(void) { return 1; }
+
+int al_device_status(unsigned* error_bits) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+  unsigned v = 0, zero = 0;
+  if ((e = cudaMemcpyFromSymbol(&v, g_al_error, sizeof(v))) != cudaSuccess) return cuda_fail(e, "cudaMemcpyFromSymbol");
+  if ((e = cudaMemcpyToSymbol(g_al_error, &zero, sizeof(zero))) != cudaSuccess) return cuda_fail(e, "cudaMemcpyToSymbol");
+  if (error_bits) *error_bits = v;
+  return AL_OK;
+}
+
+int al_sparse_decode_step(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                          const void* q_pre, int64_t qp_sb, int64_t qp_sg, int64_t qp_sh,
+                          const void* k_cache, const void* v_cache, int kv_dtype,
+                          void* zT, const void* wq_t, const void* wk, int idx_dtype,
+                          const void* k_pre_new, int64_t kn_sb, int64_t kn_sg,
+                          const int64_t* fixed_rows, const int64_t* off_lo,
+                          int B, int G, int h, int d, int r, int C,
+                          int lo, int hi, int k, int selected_count, int fixed_count, int write_col,
+                          float scale, int canonical_order,
+                          void* out, int64_t* rows_out, float* scores_out, int cluster, void* stream) {
+  DecodeParams p = {};
+  p.B = B; p.G = G; p.h = h; p.r = r; p.C = C;
+  p.lo = lo; p.hi = hi; p.k = k; p.S = selected_count; p.F = fixed_count; p.write_col = write_col;
+  p.canonical = canonical_order ? 1 : 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q_main; p.q_sb = q_sb; p.q_sg = q_sg; p.q_sh = q_sh;
+  p.q_pre = q_pre; p.qp_sb = qp_sb; p.qp_sg = qp_sg; p.qp_sh = qp_sh;
+  p.wq_t = wq_t; p.wk = wk;
+  p.k_new = k_pre_new; p.kn_sb = kn_sb; p.kn_sg = kn_sg;
+  p.zT = zT; p.k_cache = k_cache; p.v_cache = v_cache;
+  p.fixed_rows = reinterpret_cast<const long long*>(fixed_rows);
+  p.off_lo = reinterpret_cast<const long long*>(off_lo);
+  p.out = out; p.rows_out = reinterpret_cast<long long*>(rows_out); p.scores_out = scores_out;
+  return run_fused(p, kv_dtype, idx_dtype, d, cluster, stream, true);
+}
+
+int al_select_rows(const void* u, int64_t u_sb, int64_t u_sg, const void* zT, int idx_dtype,
+                   const int64_t* fixed_rows, const int64_t* off_lo,
+                   int B, int G, int r, int C, int lo, int hi, int k, int selected_count, int fixed_count,
+                   int canonical_order, int64_t* rows_out, float* scores_out, int cluster, void* stream) {
+  if (!rows_out) return fail(AL_EINVAL, "rows_out is required");
+  if (!u) return fail(AL_EINVAL, "null u");
+  if (u_sb != (int64_t)G * r || u_sg != r) return fail(AL_EINVAL, "u must be a contiguous [B,G,1,r] tensor");
+  DecodeParams p = {};
+  p.B = B; p.G = G; p.h = 1; p.r = r; p.C = C;
+  p.lo = lo; p.hi = hi; p.k = k; p.S = selected_count; p.F = fixed_count; p.write_col = -1;
+  p.canonical = canonical_order ? 1 : 0;
+  p.u_in = u;
+  p.zT = const_cast<void*>(zT);
+  p.fixed_rows = reinterpret_cast<const long long*>(fixed_rows);
+  p.off_lo = reinterpret_cast<const long long*>(off_lo);
+  p.rows_out = reinterpret_cast<long long*>(rows_out); p.scores_out = scores_out;
+  return run_fused(p, AL_BF16, idx_dtype, kHeadDim, cluster, stream, false);
+}
+
+static int run_attend(AttendParams p, int kv_dtype, int d, int n_all, int cluster, void* stream) {
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  if (!dtype_ok(kv_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (p.B <= 0 || p.G <= 0 || p.C <= 0) return fail(AL_EINVAL, "B, G and C must be positive");
+  if (p.B * (long long)p.G > 65535) return fail(AL_EUNSUPPORTED, "B*G exceeds 65535");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (p.h < 1 || p.h > 4) return fail(AL_EUNSUPPORTED, "heads per group must be in [1, 4], got %d", p.h);
+  if (!p.q || !p.k_cache || !p.v_cache || (!p.out && !p.part)) return fail(AL_EINVAL, "null pointer argument");
+  if (!aligned16(p.k_cache) || !aligned16(p.v_cache))
+    return fail(AL_EUNSUPPORTED, "k_cache and v_cache must start on a 16-byte boundary");
+  if (n_all < 1) return fail(AL_EINVAL, "at least one row must be read");
+  const long long total = (long long)p.B * p.G * p.C;
+  if (total >= 0xffffffffLL) return fail(AL_EUNSUPPORTED, "B*G*C exceeds 2^32-1 rows");
+  p.total_rows = total;
+  const int hp = pad_heads(p.h);
+  int cs = cluster;
+  if (cs <= 0) {
+    cs = 1;
+    while (cs < kMaxCluster && p.B * p.G * cs < di->sms && n_all / (cs * 2) >= 64) cs <<= 1;
+  }
+  if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
+  p.rows_cap = p.mode == 0 ? (n_all + cs - 1) / cs : 0;
+  const size_t smem = (size_t)engine_smem(kv_dtype, hp) + (size_t)p.rows_cap * 4;
+  if ((long long)smem > di->max_smem_optin - kAttendStaticBytes)
+    return fail(AL_EUNSUPPORTED, "row list too long for cluster %d (%zu bytes of shared memory)", cs, smem);
+  p.err = di->err;
+  dim3 grid((unsigned)cs, (unsigned)(p.B * p.G), 1);
+  return dispatch_attend(p, kv_dtype, hp, grid, cs, smem, stream);
+}
+
+int al_gathered_attend(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                       const void* k_cache, const void* v_cache, int kv_dtype, const int64_t* rows,
+                       int B, int G, int h, int d, int C, int selected_count, float scale,
+                       void* out, int cluster, void* stream) {
+  if (!rows) return fail(AL_EINVAL, "null rows");
+  AttendParams p = {};
+  p.B = B; p.G = G; p.h = h; p.C = C; p.S = selected_count; p.mode = 0;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q_main; p.q_sb = q_sb; p.q_sg = q_sg; p.q_sh = q_sh;
+  p.k_cache = k_cache; p.v_cache = v_cache;
+  p.rows = reinterpret_cast<const long long*>(rows);
+  p.out = out;
+  return run_attend(p, kv_dtype, d, selected_count, cluster, stream);
+}
+
+int al_dense_decode(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                    const void* k_cache, const void* v_cache, int kv_dtype,
+                    int B, int G, int h, int d, int C, int valid_length, float scale,
+                    void* out, int cluster, void* stream) {
+  if (valid_length < 1 || valid_length > C)
+    return fail(AL_EINVAL, "valid_length=%d must be in (0, capacity=%d]", valid_length, C);
+  AttendParams p = {};
+  p.B = B; p.G = G; p.h = h; p.C = C; p.L = valid_length; p.mode = 1;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q_main; p.q_sb = q_sb; p.q_sg = q_sg; p.q_sh = q_sh;
+  p.k_cache = k_cache; p.v_cache = v_cache;
+  p.out = out;
+  return run_attend(p, kv_dtype, d, valid_length, cluster, stream);
+}
+
+static unsigned grid_for(long long n) {
+  long long g = (n + kThreads - 1) / kThreads;
+  if (g > 148LL * 32) g = 148LL * 32;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
+int al_project_keys(const void* k_pre, const int64_t* kp_strides, const void* wk, int idx_dtype,
+                    int B, int G, int T, int d, int r, void* z_out, int C_out, int start, void* stream) {
+  if (!dtype_ok(idx_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (!k_pre || !kp_strides || !wk || !z_out) return fail(AL_EINVAL, "null pointer argument");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (r < 1 || r > kMaxR) return fail(AL_EUNSUPPORTED, "index width r must be in [1, %d]", kMaxR);
+  if (B <= 0 || G <= 0 || T < 0 || start < 0 || start + T > C_out)
+    return fail(AL_EINVAL, "positions [%d, %d) do not fit capacity %d", start, start + T, C_out);
+  if (T == 0) return AL_OK;
+  AppendParams p = {};
+  p.B = B; p.G = G; p.C = C_out; p.T = T; p.r = r; p.start = start;
+  p.zT = z_out; p.k_pre = k_pre; p.wk = wk;
+  for (int i = 0; i < 4; ++i) p.kp_s[i] = kp_strides[i];
+  dim3 grid((unsigned)((T + 31) / 32), (unsigned)(B * G), 1);
+  if (idx_dtype == AL_F32) project_keys_kernel<float><<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  else project_keys_kernel<__nv_bfloat16><<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return plain_launch_check("project_keys_kernel");
+}
+
+int al_append_kvz(void* k_cache, void* v_cache, int kv_dtype,
+                  const void* k_new, const int64_t* k_strides, const void* v_new, const int64_t* v_strides,
+                  int new_dtype, void* zT, int idx_dtype, const void* z_new, const int64_t* z_strides,
+                  const void* k_pre, const int64_t* kp_strides, const void* wk,
+                  int B, int G, int C, int d, int r, int start, int T, void* stream) {
+  if (!dtype_ok(kv_dtype) || !dtype_ok(new_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (!k_cache || !v_cache || !k_new || !v_new || !k_strides || !v_strides) return fail(AL_EINVAL, "null pointer argument");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (B <= 0 || G <= 0 || T < 0) return fail(AL_EINVAL, "bad shape");
+  if (start < 0 || start + T > C) return fail(AL_ESTATE, "cache capacity %d exceeded: valid %d + new %d", C, start, T);
+  if (T == 0) return AL_OK;
+  AppendParams p = {};
+  p.B = B; p.G = G; p.C = C; p.T = T; p.r = r; p.start = start;
+  p.k_cache = k_cache; p.v_cache = v_cache; p.k_new = k_new; p.v_new = v_new;
+  for (int i = 0; i < 4; ++i) { p.kn_s[i] = k_strides[i]; p.vn_s[i] = v_strides[i]; }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned grid = grid_for((long long)B * G * T * kHeadDim);
+  if (kv_dtype == AL_BF16 && new_dtype == AL_BF16) append_kv_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
+  else if (kv_dtype == AL_BF16) append_kv_kernel<__nv_bfloat16, float><<<grid, kThreads, 0, st>>>(p);
+  else if (new_dtype == AL_BF16) append_kv_kernel<float, __nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
+  else append_kv_kernel<float, float><<<grid, kThreads, 0, st>>>(p);
+  int rc = plain_launch_check("append_kv_kernel");
+  if (rc) return rc;
+  if (z_new || k_pre) {
+    if (!zT || !dtype_ok(idx_dtype)) return fail(AL_ESTATE, "this cache was created without an index table");
+    if (r < 1 || r > kMaxR) return fail(AL_EUNSUPPORTED, "index width r must be in [1, %d]", kMaxR);
+    p.zT = zT;
+    if (z_new) {
+      if (!z_strides) return fail(AL_EINVAL, "null z strides");
+      p.z_new = z_new;
+      for (int i = 0; i < 4; ++i) p.zn_s[i] = z_strides[i];
+      const unsigned gz = grid_for((long long)B * G * r * T);
+      if (idx_dtype == AL_F32) append_z_copy_kernel<float, float><<<gz, kThreads, 0, st>>>(p);
+      else append_z_copy_kernel<__nv_bfloat16, __nv_bfloat16><<<gz, kThreads, 0, st>>>(p);
+      return plain_launch_check("append_z_copy_kernel");
+    }
+    if (!wk || !kp_strides) return fail(AL_EINVAL, "k_pre given without wk or strides");
+    return al_project_keys(k_pre, kp_strides, wk, idx_dtype, B, G, T, d, r, zT, C, start, stream);
+  }
+  return AL_OK;
+}
+
+int al_project_queries(const void* q_pre, const int64_t* qp_strides, const void* wq_t, int idx_dtype,
+                       int B, int G, int h, int T, int d, int r, void* u_out, int out_f32, void* stream) {
+  if (!dtype_ok(idx_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (!q_pre || !qp_strides || !wq_t || !u_out) return fail(AL_EINVAL, "null pointer argument");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (r < 1 || r > kMaxR) return fail(AL_EUNSUPPORTED, "index width r must be in [1, %d]", kMaxR);
+  if (B <= 0 || G <= 0 || h <= 0 || T <= 0) return fail(AL_EINVAL, "bad shape");
+  IndexParams p = {};
+  p.B = B; p.G = G; p.h = h; p.T = T; p.r = r;
+  p.q_pre = q_pre; p.wq_t = wq_t; p.out = u_out; p.out_f32 = out_f32 ? 1 : 0;
+  for (int i = 0; i < 5; ++i) p.qp_s[i] = qp_strides[i];
+  const unsigned grid = (unsigned)(B * G * T);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (idx_dtype == AL_F32) project_queries_kernel<float><<<grid, kThreads, 0, st>>>(p);
+  else project_queries_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
+  return plain_launch_check("project_queries_kernel");
+}
+
+int al_candidate_scores(const void* u, const int64_t* u_strides, const void* zT, int idx_dtype,
+                        int B, int G, int T, int r, int C, int lo, int hi, void* out, int out_f32, void* stream) {
+  if (!dtype_ok(idx_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (!u || !u_strides || !zT || !out) return fail(AL_EINVAL, "null pointer argument");
+  if (r < 1 || r > kMaxR) return fail(AL_EUNSUPPORTED, "index width r must be in [1, %d]", kMaxR);
+  if (B <= 0 || G <= 0 || T <= 0) return fail(AL_EINVAL, "bad shape");
+  if (!(0 <= lo && lo <= hi && hi <= C)) return fail(AL_EINVAL, "need 0 <= lo <= hi <= C");
+  if (hi == lo) return AL_OK;
+  IndexParams p = {};
+  p.B = B; p.G = G; p.T = T; p.r = r; p.C = C; p.lo = lo; p.hi = hi;
+  p.u = u; p.zT = zT; p.out = out; p.out_f32 = out_f32 ? 1 : 0;
+  for (int i = 0; i < 4; ++i) p.u_s[i] = u_strides[i];
+  dim3 grid((unsigned)((hi - lo + kThreads - 1) / kThreads), (unsigned)(B * G * T), 1);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (idx_dtype == AL_F32) candidate_scores_kernel<float><<<grid, kThreads, 0, st>>>(p);
+  else candidate_scores_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
+  return plain_launch_check("candidate_scores_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,96 @@
+// Device helpers shared by every kernel of the sparse-decode library (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cooperative_groups.h>
+#include <stdint.h>
+
+namespace al {
+namespace cg = cooperative_groups;
+
+constexpr int kThreads = 256;              // threads per CTA for every decode kernel
+constexpr int kWarps = kThreads / 32;
+constexpr int kHeadDim = 128;              // d: 8 lanes x 16 dims per K/V row
+constexpr int kMaxR = 32;                  // index width r
+constexpr int kMaxCluster = 16;            // CTAs per (batch, group) segment
+
+// Error bits OR-ed into g_al_error by kernels (read and cleared by al_device_status()).
+constexpr unsigned kErrRowRange = 1u;      // a row id outside [0, B*G*C) was skipped
+constexpr unsigned kErrCluster = 2u;       // launch shape did not match the cluster the kernel expects
+
+// ------------------------------------------------------------------------------------------------ conversions
+template <typename T> __device__ __forceinline__ float tof(T x);
+template <> __device__ __forceinline__ float tof<float>(float x) { return x; }
+template <> __device__ __forceinline__ float tof<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+
+template <typename T> __device__ __forceinline__ T fromf(float x);
+template <> __device__ __forceinline__ float fromf<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 fromf<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+
+// Elements of T in one 16-byte vector.
+template <typename T> struct V16 { static constexpr int n = 16 / (int)sizeof(T); };
+
+// Unpack a 16-byte vector of T into floats (bf16 -> fp32 is a 16-bit shift, exact).
+__device__ __forceinline__ void unpack(const uint4& v, float* f, const __nv_bfloat16*) {
+  f[0] = __uint_as_float(v.x << 16); f[1] = __uint_as_float(v.x & 0xffff0000u);
+  f[2] = __uint_as_float(v.y << 16); f[3] = __uint_as_float(v.y & 0xffff0000u);
+  f[4] = __uint_as_float(v.z << 16); f[5] = __uint_as_float(v.z & 0xffff0000u);
+  f[6] = __uint_as_float(v.w << 16); f[7] = __uint_as_float(v.w & 0xffff0000u);
+}
+__device__ __forceinline__ void unpack(const uint4& v, float* f, const float*) {
+  f[0] = __uint_as_float(v.x); f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z); f[3] = __uint_as_float(v.w);
+}
+
+// 16-byte read-only global load that does not allocate in L1 (streamed data).
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+
+// Order-preserving map float -> uint32: a > b  <=>  key(a) > key(b). -0 maps to +0, every NaN ranks above +inf
+// (the convention of torch.topk, which treats NaN as the largest value).
+__device__ __forceinline__ uint32_t score_key(float s) {
+  if (s != s) return 0xffffffffu;
+  if (s == 0.0f) s = 0.0f;
+  const uint32_t u = __float_as_uint(s);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// ------------------------------------------------------------------------------------------------ cp.async
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ------------------------------------------------------------------------------------------------ block scans
+// Inclusive prefix sum of one int per thread over the whole CTA. `ws` holds kWarps ints of shared scratch.
+// Returns the inclusive sum; *total receives the CTA total. Contains two __syncthreads().
+__device__ __forceinline__ int block_inclusive_scan(int v, int* ws, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) ws[w] = v;
+  __syncthreads();
+  int before = 0, tot = 0;
+#pragma unroll
+  for (int i = 0; i < kWarps; ++i) {
+    const int x = ws[i];
+    before += (i < w) ? x : 0;
+    tot += x;
+  }
+  __syncthreads();
+  *total = tot;
+  return v + before;
+}
+
+}  // namespace al

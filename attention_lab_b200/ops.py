@@ -1,0 +1,310 @@
+"""Drop-in operators for attention-lab's sparse-decode path, backed by the sm_100a C-ABI library.
+
+Names, argument order, argument meaning, return values and exception types follow the reference's operators:
+
+    sparse_decode_step_kernel   decode.py:145-163      fused: z column, u, scores, top-k, F merge, attend
+    select_rows_kernel          decode.py:86-93        scores + top-k + F merge -> flat int64 rows [B*G*S]
+    gathered_decode_step_kernel decode.py:131-142      attention over listed flat rows, read in place
+    dense_decode_step           decode.py:174-176      dense read of [0, valid_length) for one query
+    candidate_scores            indexer.py:27-29
+    project_keys                indexer.py:15-17
+    project_queries             indexer.py:20-24
+    append_kvz                  qwen_wrap.py:90-106    the K/V (+ index column) write of LabCache.append
+
+Every tensor must live on a CUDA device; float32 and bfloat16 are supported, head_dim must be 128 and the index
+width at most 32. The work is enqueued on the current CUDA stream of the tensors' device and nothing synchronises.
+Differences from the reference that do not change results: top-k ties go to the smaller position (torch.topk leaves
+them unspecified), and the chosen candidates follow F in ascending position order rather than in descending score
+order (the set, and every attention output, is the same; with canonical_order both paths sort every list).
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.AL_F32, torch.bfloat16: _lib.AL_BF16}
+SUBSET_BACKENDS = ("sdpa", "explicit")
+FULL_BACKENDS = ("sdpa_fold", "sdpa_gqa", "sdpa_repeat", "explicit")
+
+
+def _code(t: torch.Tensor, what: str) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise ValueError(f"{what} must be float32 or bfloat16 on the CUDA path, got {t.dtype}") from None
+
+
+def _cuda(*ts):
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("every tensor must live on a CUDA device (the CUDA path has no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all inputs must live on the same device")
+    return dev
+
+
+def _stream(dev) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _scale(d: int, scale) -> float:
+    return 1.0 / math.sqrt(d) if scale is None else float(scale)
+
+
+def _check_cache(x: torch.Tensor, what: str):
+    if x.dim() != 4:
+        raise ValueError(f"{what} must be [B,G,C,d], got {tuple(x.shape)}")
+    if not x.is_contiguous():
+        raise ValueError(f"{what} must be contiguous so the flattened view is free")
+
+
+def _q_strides(q: torch.Tensor, what: str):
+    if q.dim() != 5:
+        raise ValueError(f"{what} must be [B,G,h,T,d], got {tuple(q.shape)}")
+    if q.shape[3] != 1:
+        raise ValueError("a decode step takes exactly one new query position")
+    if q.stride(4) != 1:
+        q = q.contiguous()
+    return q, q.stride(0), q.stride(1), q.stride(2)
+
+
+def _check_backend(backend: str, allowed):
+    if backend not in allowed:
+        raise ValueError(f"unknown backend {backend!r}; choose from {allowed}")
+
+
+def sparse_decode_step_kernel(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, fixed_rows, off_lo, lo: int,
+                              hi: int, k: int, selected_count: int, *, k_pre_new=None, write_col: int = -1,
+                              scale=None, backend="sdpa", return_rows: bool = False, canonical_order: bool = False,
+                              cluster: int = 0, scores_out=None):
+    """One layer's D read for one new query (T == 1), as one kernel launch. Writes z of the newest key into
+    zT[..., write_col] when k_pre_new is given. Returns out [B,G,h,1,d] (and flat int64 rows [B*G*S] with
+    return_rows). `cluster` (CTAs per (batch, group), 0 = automatic) and `scores_out` (fp32 [B,G,hi-lo] scores)
+    are extensions for tuning and diagnostics."""
+    _check_backend(backend, SUBSET_BACKENDS)
+    dev = _cuda(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, fixed_rows, off_lo, k_pre_new)
+    q_main, qsb, qsg, qsh = _q_strides(q_main, "q_main")
+    q_pre, psb, psg, psh = _q_strides(q_pre, "q_pre")
+    B, G, h, _, d = q_main.shape
+    _check_cache(k_cache, "k_cache")
+    _check_cache(v_cache, "v_cache")
+    if k_cache.shape != v_cache.shape or k_cache.shape[0] != B or k_cache.shape[1] != G or k_cache.shape[3] != d:
+        raise ValueError(f"shape mismatch: q {tuple(q_main.shape)} k {tuple(k_cache.shape)} v {tuple(v_cache.shape)}")
+    kv = _code(q_main, "q_main")
+    if k_cache.dtype != q_main.dtype or v_cache.dtype != q_main.dtype:
+        raise ValueError("q_main, k_cache and v_cache must share one dtype")
+    C = k_cache.shape[2]
+    if zT.dim() != 4 or zT.shape[0] != B or zT.shape[1] != G or zT.shape[3] != C or not zT.is_contiguous():
+        raise ValueError("zT must be a contiguous [B,G,r,C] tensor matching the cache")
+    r = zT.shape[2]
+    idx = _code(zT, "zT")
+    for t, what in ((q_pre, "q_pre"), (wq_t_scaled, "wq_t_scaled"), (wk, "wk"), (k_pre_new, "k_pre_new")):
+        if t is not None and t.dtype != zT.dtype:
+            raise ValueError(f"{what} must have the index dtype {zT.dtype}, got {t.dtype}")
+    if tuple(q_pre.shape) != (B, G, h, 1, d):
+        raise ValueError("q_pre must match q_main's shape")
+    if tuple(wq_t_scaled.shape) != (G, h * d, r) or tuple(wk.shape) != (G, r, d):
+        raise ValueError("wq_t_scaled must be [G,h*d,r] and wk [G,r,d]")
+    wq_t_scaled, wk = wq_t_scaled.contiguous(), wk.contiguous()
+    F = int(fixed_rows.shape[-1])
+    if tuple(fixed_rows.shape) != (B, G, F) or fixed_rows.dtype != torch.int64:
+        raise ValueError("fixed_rows must be int64 [B,G,F]")
+    if off_lo.numel() != B * G or off_lo.dtype != torch.int64:
+        raise ValueError("off_lo must be int64 [B,G,1]")
+    fixed_rows, off_lo = fixed_rows.contiguous(), off_lo.contiguous()
+    kn_sb = kn_sg = 0
+    if k_pre_new is not None:
+        if tuple(k_pre_new.shape) != (B, G, 1, d):
+            raise ValueError("k_pre_new must be [B,G,1,d]")
+        if k_pre_new.stride(3) != 1:
+            k_pre_new = k_pre_new.contiguous()
+        kn_sb, kn_sg = k_pre_new.stride(0), k_pre_new.stride(1)
+    out = torch.empty((B, G, h, 1, d), dtype=q_main.dtype, device=dev)
+    rows = torch.empty(B * G * selected_count, dtype=torch.int64, device=dev) if return_rows else None
+    if scores_out is not None and (scores_out.dtype != torch.float32 or not scores_out.is_contiguous()
+                                   or scores_out.numel() != B * G * max(hi - lo, 0)):
+        raise ValueError("scores_out must be a contiguous float32 tensor of B*G*(hi-lo) elements")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.al_sparse_decode_step(
+            q_main.data_ptr(), qsb, qsg, qsh, q_pre.data_ptr(), psb, psg, psh,
+            k_cache.data_ptr(), v_cache.data_ptr(), kv, zT.data_ptr(), wq_t_scaled.data_ptr(), wk.data_ptr(), idx,
+            _ptr(k_pre_new), kn_sb, kn_sg, fixed_rows.data_ptr(), off_lo.data_ptr(),
+            B, G, h, d, r, C, int(lo), int(hi), int(k), int(selected_count), F, int(write_col),
+            _scale(d, scale), int(bool(canonical_order)), out.data_ptr(), _ptr(rows), _ptr(scores_out),
+            int(cluster), _stream(dev)))
+    return (out, rows) if return_rows else out
+
+
+def select_rows_kernel(u, zT, fixed_rows, off_lo, lo: int, hi: int, k: int, *, canonical_order: bool = False,
+                       cluster: int = 0) -> torch.Tensor:
+    """D0 selection: one scan of the candidate columns, one top-k, merge with the fixed rows -> flat rows
+    [B*G*S] (decode.py:86-93)."""
+    B, G = fixed_rows.shape[:2]
+    if k <= 0:
+        return fixed_rows.reshape(-1)
+    dev = _cuda(u, zT, fixed_rows, off_lo)
+    if u.dim() != 4 or u.shape[2] != 1:
+        raise ValueError("u must be [B,G,1,r]")
+    if zT.dim() != 4 or not zT.is_contiguous() or u.dtype != zT.dtype:
+        raise ValueError("zT must be a contiguous [B,G,r,C] tensor of u's dtype")
+    idx = _code(zT, "zT")
+    r, C = zT.shape[2], zT.shape[3]
+    F = int(fixed_rows.shape[-1])
+    if fixed_rows.dtype != torch.int64 or off_lo.dtype != torch.int64:
+        raise ValueError("fixed_rows and off_lo must be int64")
+    u, fixed_rows, off_lo = u.contiguous(), fixed_rows.contiguous(), off_lo.contiguous()
+    S = F + int(k)
+    rows = torch.empty(B * G * S, dtype=torch.int64, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_select_rows(
+            u.data_ptr(), G * r, r, zT.data_ptr(), idx, fixed_rows.data_ptr(), off_lo.data_ptr(),
+            B, G, r, C, int(lo), int(hi), int(k), S, F, int(bool(canonical_order)), rows.data_ptr(), None,
+            int(cluster), _stream(dev)))
+    return rows
+
+
+def gathered_decode_step_kernel(q_main, k_cache, v_cache, rows, selected_count: int, *, scale=None, backend="sdpa",
+                                cluster: int = 0):
+    """Read exactly the listed flat rows of K and V in place and attend over them (decode.py:131-142)."""
+    _check_backend(backend, SUBSET_BACKENDS)
+    dev = _cuda(q_main, k_cache, v_cache, rows)
+    q_main, qsb, qsg, qsh = _q_strides(q_main, "q_main")
+    B, G, h, _, d = q_main.shape
+    _check_cache(k_cache, "k_cache")
+    _check_cache(v_cache, "v_cache")
+    if k_cache.dtype != q_main.dtype or v_cache.dtype != q_main.dtype or k_cache.shape != v_cache.shape:
+        raise ValueError("q_main, k_cache and v_cache must share one dtype and K/V one shape")
+    if rows.dtype != torch.int64 or rows.numel() != B * G * selected_count:
+        raise ValueError("rows must be int64 flat row ids [B*G*selected_count]")
+    kv = _code(q_main, "q_main")
+    rows = rows.contiguous()
+    out = torch.empty((B, G, h, 1, d), dtype=q_main.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_gathered_attend(
+            q_main.data_ptr(), qsb, qsg, qsh, k_cache.data_ptr(), v_cache.data_ptr(), kv, rows.data_ptr(),
+            B, G, h, d, k_cache.shape[2], int(selected_count), _scale(d, scale), out.data_ptr(), int(cluster),
+            _stream(dev)))
+    return out
+
+
+def dense_decode_step(q_main, k_cache, v_cache, valid_length: int, *, backend="sdpa_fold", scale=None,
+                      cluster: int = 0):
+    """A read for one new query at the end of the legal range: every position [0, valid_length) (decode.py:174-176,
+    full.py:17-45). Every reference backend computes the same function; the CUDA path has one kernel."""
+    _check_backend(backend, FULL_BACKENDS)
+    dev = _cuda(q_main, k_cache, v_cache)
+    q_main, qsb, qsg, qsh = _q_strides(q_main, "q_main")
+    B, G, h, _, d = q_main.shape
+    _check_cache(k_cache, "k_cache")
+    _check_cache(v_cache, "v_cache")
+    if k_cache.dtype != q_main.dtype or v_cache.dtype != q_main.dtype or k_cache.shape != v_cache.shape:
+        raise ValueError("q_main, k_cache and v_cache must share one dtype and K/V one shape")
+    kv = _code(q_main, "q_main")
+    out = torch.empty((B, G, h, 1, d), dtype=q_main.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_dense_decode(
+            q_main.data_ptr(), qsb, qsg, qsh, k_cache.data_ptr(), v_cache.data_ptr(), kv,
+            B, G, h, d, k_cache.shape[2], int(valid_length), _scale(d, scale), out.data_ptr(), int(cluster),
+            _stream(dev)))
+    return out
+
+
+def project_keys(k_pre: torch.Tensor, wk: torch.Tensor) -> torch.Tensor:
+    """k_pre [B,G,C,d], wk [G,r,d] -> zT [B,G,r,C] (indexer.py:15-17), in k_pre's dtype."""
+    dev = _cuda(k_pre, wk)
+    if k_pre.dim() != 4 or wk.dim() != 3 or k_pre.dtype != wk.dtype:
+        raise ValueError("k_pre must be [B,G,C,d] and wk [G,r,d] of one dtype")
+    B, G, T, d = k_pre.shape
+    r = wk.shape[1]
+    idx = _code(k_pre, "k_pre")
+    wk = wk.contiguous()
+    z = torch.empty((B, G, r, T), dtype=k_pre.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_project_keys(k_pre.data_ptr(), _lib.strides(k_pre, 4), wk.data_ptr(), idx,
+                                               B, G, T, d, r, z.data_ptr(), T, 0, _stream(dev)))
+    return z
+
+
+def project_queries(q_pre: torch.Tensor, wq_t_scaled: torch.Tensor) -> torch.Tensor:
+    """q_pre [B,G,h,T,d], wq_t_scaled [G,h*d,r] -> u [B,G,T,r] (indexer.py:20-24), in q_pre's dtype."""
+    dev = _cuda(q_pre, wq_t_scaled)
+    if q_pre.dim() != 5 or wq_t_scaled.dim() != 3 or q_pre.dtype != wq_t_scaled.dtype:
+        raise ValueError("q_pre must be [B,G,h,T,d] and wq_t_scaled [G,h*d,r] of one dtype")
+    B, G, h, T, d = q_pre.shape
+    r = wq_t_scaled.shape[2]
+    idx = _code(q_pre, "q_pre")
+    wq = wq_t_scaled.contiguous()
+    u = torch.empty((B, G, T, r), dtype=q_pre.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_project_queries(q_pre.data_ptr(), _lib.strides(q_pre, 5), wq.data_ptr(), idx,
+                                                  B, G, h, T, d, r, u.data_ptr(), 0, _stream(dev)))
+    return u
+
+
+def candidate_scores(u: torch.Tensor, zT: torch.Tensor, lo: int, hi: int, *, out_dtype=None) -> torch.Tensor:
+    """u [B,G,T,r] against the candidate columns only -> [B,G,T,hi-lo] (indexer.py:27-29). Accumulates in fp32;
+    the result has u's dtype (as torch.matmul's) unless out_dtype=torch.float32."""
+    dev = _cuda(u, zT)
+    if u.dim() != 4 or zT.dim() != 4 or not zT.is_contiguous() or u.dtype != zT.dtype:
+        raise ValueError("u must be [B,G,T,r] and zT a contiguous [B,G,r,C] tensor of the same dtype")
+    B, G, T, r = u.shape
+    C = zT.shape[3]
+    idx = _code(zT, "zT")
+    f32 = out_dtype == torch.float32
+    out = torch.empty((B, G, T, max(hi - lo, 0)), dtype=torch.float32 if f32 else u.dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_candidate_scores(u.data_ptr(), _lib.strides(u, 4), zT.data_ptr(), idx,
+                                                   B, G, T, r, C, int(lo), int(hi), out.data_ptr(), int(f32),
+                                                   _stream(dev)))
+    return out
+
+
+def append_kvz(k_cache, v_cache, zT, start: int, k_new, v_new, z_new=None, *, k_pre=None, wk=None) -> None:
+    """Write T new rows at positions [start, start+T) of K/V [B,G,C,d] and, when given, index columns of zT
+    [B,G,r,C]: either the values z_new [B,G,r,T] or Wk . k_pre computed in the same launch sequence (the prefill
+    index build). The K/V part of LabCache.append (qwen_wrap.py:90-106)."""
+    dev = _cuda(k_cache, v_cache, zT, k_new, v_new, z_new, k_pre, wk)
+    _check_cache(k_cache, "k_cache")
+    _check_cache(v_cache, "v_cache")
+    B, G, C, d = k_cache.shape
+    if k_new.dim() != 4 or tuple(k_new.shape[:2]) != (B, G) or k_new.shape[3] != d or v_new.shape != k_new.shape:
+        raise ValueError("k_new and v_new must be [B,G,T,d] matching the cache")
+    if v_new.dtype != k_new.dtype:
+        raise ValueError("k_new and v_new must share one dtype")
+    T = k_new.shape[2]
+    kv, nd = _code(k_cache, "k_cache"), _code(k_new, "k_new")
+    idx, r = 0, 0
+    zs = kps = None
+    if z_new is not None or k_pre is not None:
+        if zT is None:
+            raise RuntimeError("this cache was created without an index table")
+        idx, r = _code(zT, "zT"), zT.shape[2]
+        if z_new is not None:
+            if tuple(z_new.shape) != (B, G, r, T) or z_new.dtype != zT.dtype:
+                raise ValueError("z_new must be [B,G,r,T] in the index dtype")
+            zs = _lib.strides(z_new, 4)
+        else:
+            if wk is None or k_pre.dtype != zT.dtype or wk.dtype != zT.dtype:
+                raise ValueError("k_pre and wk must be given in the index dtype")
+            if tuple(k_pre.shape) != (B, G, T, d):
+                raise ValueError("k_pre must be [B,G,T,d]")
+            wk = wk.contiguous()
+            kps = _lib.strides(k_pre, 4)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_append_kvz(
+            k_cache.data_ptr(), v_cache.data_ptr(), kv, k_new.data_ptr(), _lib.strides(k_new, 4), v_new.data_ptr(),
+            _lib.strides(v_new, 4), nd, _ptr(zT), idx, _ptr(z_new), zs, _ptr(k_pre), kps, _ptr(wk),
+            B, G, C, d, r, int(start), T, _stream(dev)))

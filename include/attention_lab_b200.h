@@ -1,0 +1,117 @@
+/*
+ * attention_lab_b200 -- C ABI of the B200 (sm_100a) sparse-decode hot path of attention-lab.
+ *
+ * Every entry point takes plain device pointers, sizes, element strides, dtype codes and a CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream). Nothing allocates, nothing synchronises the host,
+ * launches are asynchronous on the given stream, and every call returns a status code (never throws).
+ * `al_last_error()` returns the message of the last failing call on the calling thread.
+ *
+ * Shapes use the reference's conventions (attention-lab docs/IMPLEMENTATION.md):
+ *   B batch, G KV groups, h query heads per group, d head dim (= 128), r index width (<= 32), C cache capacity,
+ *   caches K/V [B,G,C,d] and index table zT [B,G,r,C], both contiguous; a flat row id is (b*G+g)*C + position.
+ * Element strides are in elements of the tensor's own dtype; the innermost (d) stride must be 1 where not listed.
+ */
+#ifndef ATTENTION_LAB_B200_H
+#define ATTENTION_LAB_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define AL_OK 0
+#define AL_EINVAL 1       /* invalid shape, dtype, layout or range: the reference raises ValueError */
+#define AL_ESTATE 2       /* state / order violation: the reference raises RuntimeError */
+#define AL_ECUDA 3        /* the CUDA runtime reported an error at launch */
+#define AL_EUNSUPPORTED 4 /* valid for the reference but outside what these kernels implement (ValueError) */
+
+/* dtype codes */
+#define AL_F32 0
+#define AL_BF16 1
+
+/* Message of the last failing call on this thread ("" when none). */
+const char* al_last_error(void);
+
+/* ABI version of this library. */
+int al_version(void);
+
+/* Synchronises the current device, then returns (and clears) the error bits kernels raised since the last call:
+ * 1 = a row id outside [0, B*G*C) was skipped, 2 = a launch had an unexpected cluster shape. */
+int al_device_status(unsigned* error_bits);
+
+/* a8: one layer's sparse decode step, fused into one launch (replaces attention-lab
+ * src/attention_lab/decode.py:145-163 `sparse_decode_step_kernel`).
+ *   q_main [B,G,h,1,d] (kv dtype), q_pre [B,G,h,1,d] (idx dtype): strides for B, G, h.
+ *   k_pre_new [B,G,1,d] (idx dtype) or NULL: when given, z = Wk . k_pre_new is written to zT[..., write_col] first
+ *   (decode.py:156-157); write_col must lie outside [lo, hi).
+ *   wq_t [G,h*d,r] (1/sqrt(r) folded in), wk [G,r,d]: idx dtype, contiguous.
+ *   fixed_rows [B,G,fixed_count] int64 flat rows of F; off_lo [B,G,1] int64 flat row of candidate 0.
+ *   selected_count = fixed_count + k; 0 <= k <= hi - lo.
+ *   out [B,G,h,d] (kv dtype, contiguous). rows_out [B,G,selected_count] int64 flat rows or NULL: F first, then the
+ *   chosen candidates in ascending position order; with canonical_order every group's list is ascending
+ *   (decode.py:160-161). scores_out [B,G,hi-lo] fp32 or NULL.
+ *   Top-k ties are broken towards the smaller position. cluster: CTAs per (b,g) (0 = automatic, else 1..16). */
+int al_sparse_decode_step(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                          const void* q_pre, int64_t qp_sb, int64_t qp_sg, int64_t qp_sh,
+                          const void* k_cache, const void* v_cache, int kv_dtype,
+                          void* zT, const void* wq_t, const void* wk, int idx_dtype,
+                          const void* k_pre_new, int64_t kn_sb, int64_t kn_sg,
+                          const int64_t* fixed_rows, const int64_t* off_lo,
+                          int B, int G, int h, int d, int r, int C,
+                          int lo, int hi, int k, int selected_count, int fixed_count, int write_col,
+                          float scale, int canonical_order,
+                          void* out, int64_t* rows_out, float* scores_out, int cluster, void* stream);
+
+/* a5: score the candidate columns with a given u and select (replaces decode.py:86-93 `select_rows_kernel`).
+ *   u [B,G,1,r] (idx dtype, strides for B, G). Output rows_out [B,G,selected_count] int64 (required). */
+int al_select_rows(const void* u, int64_t u_sb, int64_t u_sg, const void* zT, int idx_dtype,
+                   const int64_t* fixed_rows, const int64_t* off_lo,
+                   int B, int G, int r, int C, int lo, int hi, int k, int selected_count, int fixed_count,
+                   int canonical_order, int64_t* rows_out, float* scores_out, int cluster, void* stream);
+
+/* a7: attention over listed flat rows, read in place (replaces decode.py:131-142 `gathered_decode_step_kernel`).
+ *   rows [B,G,selected_count] int64 flat rows (any order; duplicates are read twice, as index_select does). */
+int al_gathered_attend(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                       const void* k_cache, const void* v_cache, int kv_dtype, const int64_t* rows,
+                       int B, int G, int h, int d, int C, int selected_count, float scale,
+                       void* out, int cluster, void* stream);
+
+/* a11: dense decode read over positions [0, valid_length) (replaces decode.py:174-176 `dense_decode_step` for a
+ *   single query at the end of the legal range, full.py:17-45 `sdpa_fold`). */
+int al_dense_decode(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                    const void* k_cache, const void* v_cache, int kv_dtype,
+                    int B, int G, int h, int d, int C, int valid_length, float scale,
+                    void* out, int cluster, void* stream);
+
+/* a1: cache append (replaces qwen_wrap.py:90-106 `LabCache.append`): K/V rows [B,G,T,d] (4 strides each, dtype
+ *   new_dtype, cast to kv_dtype) go to positions [start, start+T). The index columns [start, start+T) of zT are
+ *   written from z_new [B,G,r,T] (4 strides, idx dtype) when given, else computed as Wk . k_pre (k_pre [B,G,T,d],
+ *   4 strides, idx dtype; the prefill index build, qwen_wrap.py:320-324) when k_pre and wk are given. */
+int al_append_kvz(void* k_cache, void* v_cache, int kv_dtype,
+                  const void* k_new, const int64_t* k_strides, const void* v_new, const int64_t* v_strides,
+                  int new_dtype, void* zT, int idx_dtype, const void* z_new, const int64_t* z_strides,
+                  const void* k_pre, const int64_t* kp_strides, const void* wk,
+                  int B, int G, int C, int d, int r, int start, int T, void* stream);
+
+/* a2: index keys (replaces indexer.py:15-17 `project_keys`): z_out [B,G,r,C_out] columns [start, start+T) =
+ *   wk[g] . k_pre[b,g,t] with k_pre [B,G,T,d] (4 strides). */
+int al_project_keys(const void* k_pre, const int64_t* kp_strides, const void* wk, int idx_dtype,
+                    int B, int G, int T, int d, int r, void* z_out, int C_out, int start, void* stream);
+
+/* a3: index query (replaces indexer.py:20-24 `project_queries`): u [B,G,T,r] (contiguous) from q_pre [B,G,h,T,d]
+ *   (5 strides) and wq_t [G,h*d,r]; written in idx dtype, or fp32 when out_f32. */
+int al_project_queries(const void* q_pre, const int64_t* qp_strides, const void* wq_t, int idx_dtype,
+                       int B, int G, int h, int T, int d, int r, void* u_out, int out_f32, void* stream);
+
+/* a4: candidate scores (replaces indexer.py:27-29 `candidate_scores`): out [B,G,T,hi-lo] (contiguous) =
+ *   u [B,G,T,r] (4 strides) . zT[..., lo:hi]; written in idx dtype, or fp32 when out_f32. */
+int al_candidate_scores(const void* u, const int64_t* u_strides, const void* zT, int idx_dtype,
+                        int B, int G, int T, int r, int C, int lo, int hi, void* out, int out_f32, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTENTION_LAB_B200_H */
