@@ -1,0 +1,477 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 sparse-decode hot path (attention-lab's score -> top-k -> attend, plus the cache append).
+
+Workload (default `c3`, the configuration the headline metric is quoted on: 32K context): a Qwen3-8B-shape decode
+step of the hot path over every layer: 36 layers, B = 32 requests per GPU, G = 8 KV groups, h = 4 query heads per
+group, d = 128, r = 32, legal length L = 32768, rho = 1/32 (k = 1024, S = 1092), bf16 K/V and bf16 index keys (the
+reference's default index layout), random synthetic data (no checkpoint or dataset is involved in this path).
+One step = for every layer: the K/V append of the new token, then the fused sparse step (z column, u, candidate
+scores, top-k, F merge, gather-free attention). Every layer has its own cache, so nothing stays in L2 between layers
+(each fused launch reads 679 MB).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c3|c2|c4|c1]
+
+Under torchrun every rank runs the same per-GPU workload on its own requests (request sharding, no collective on
+the data path: weak scaling); the timed region is bracketed by barriers and synchronisations, its device time is the
+max over ranks, and rank 0 prints one JSON line. `--impl reference` times the CPU restatement of the reference's
+path (oracle/oracle.py) on the host cores and prints the reference arm's line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    # name: (layers, B, G, h, L, rho, description)
+    "c3": (36, 32, 8, 4, 32768, 1 / 32, "C3: Qwen3-8B-shape hot path, 36 layers, B=32 per GPU, L=32768, rho=1/32"),
+    "c2": (28, 1, 8, 2, 8193, 1 / 32, "C2: Qwen3-0.6B-shape hot path, 28 layers, B=1, L=8193, rho=1/32"),
+    "c4": (1, 1, 8, 4, 131072, 1 / 32, "C4: one Qwen3-8B-shape layer, B=1, L=131072, rho=1/32"),
+    "c1": (1, 1, 8, 2, 2048, 1 / 32, "C1: one Qwen3-0.6B-shape layer, B=1, L=2048, rho=1/32"),
+}
+D, R = 128, 32
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c3")
+    ap.add_argument("--index-dtype", choices=["bf16", "f32"], default="bf16")
+    ap.add_argument("--cluster", type=int, default=0, help="CTAs per (batch, group); 0 = automatic")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-baselines", action="store_true", help="skip the same-box dense / torch reference timings")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of the CPU baseline sample")
+    ap.add_argument("--batch", type=int, default=0, help="override the workload's requests per GPU (profiling cases)")
+    ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling cases)")
+    return ap.parse_args()
+
+
+def workload(args):
+    layers, B, G, h, L, rho, desc = WORKLOADS[args.workload]
+    if args.batch or args.layers:
+        layers, B = args.layers or layers, args.batch or B
+        desc += f" [profiling override: B={B}, layers={layers}]"
+    return layers, B, G, h, L, rho, desc
+
+
+def ledger(B, G, h, L, rho, layers, zb, eb):
+    """Algorithmic bytes from the reference's ledger terms (scripts/roofline.py:61-74, scan_scope=candidates),
+    per (layer, request): score = G*r*M*zb, attend = S*G*d*2*eb."""
+    from attention_lab_b200.selection import fixed_budget, selection_layout
+    lay = selection_layout(L)
+    k = lay.clamp_k(fixed_budget(L, rho))
+    M, S = lay.candidate_count, lay.fixed_count + k
+    score = G * R * M * zb
+    attend = S * G * D * 2 * eb
+    return {"k": k, "S": S, "M": M, "lo": lay.candidate_lo, "hi": lay.candidate_hi, "F": lay.fixed_count,
+            "score_bytes": score, "attend_bytes": attend, "d_s1_per_layer_request": score + attend,
+            "per_launch": B * (score + attend), "dense_kv_per_layer_request": 2 * G * L * D * eb}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region (every 100 ms)."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def measured_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, STREAM-style copy)"
+    return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
+
+
+# ------------------------------------------------------------------------------------------------ CPU side
+def cpu_sample(args, B, G, h, L, rho, layers, budget_s):
+    """Time the CPU restatement of the reference's step (oracle.cpu_sparse_request, float32 numpy) on a bounded
+    sample: P requests of one layer in parallel (one per worker thread), repeated until ~budget_s of wall time.
+    Returns tokens/s of the full workload (B requests x layers layers) extrapolated from the per-request cost."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from threadpoolctl import threadpool_limits
+    from oracle import oracle as orc
+    lg = ledger(B, G, h, L, rho, layers, 2, 2)
+    workers = max(1, min(64, os.cpu_count() or 1))
+    rng = np.random.default_rng(0)
+    C = L
+    K = rng.standard_normal((G, C, D), dtype=np.float32)
+    V = rng.standard_normal((G, C, D), dtype=np.float32)
+    zT = rng.standard_normal((G, R, C), dtype=np.float32)
+    wq = (rng.standard_normal((G, h * D, R), dtype=np.float32) * 0.02)
+    wk = (rng.standard_normal((G, R, D), dtype=np.float32) * 0.02)
+    reqs = [(rng.standard_normal((G, h, D), dtype=np.float32), rng.standard_normal((G, h, D), dtype=np.float32),
+             rng.standard_normal((G, D), dtype=np.float32)) for _ in range(workers)]
+    zTs = [zT.copy() for _ in range(workers)]
+
+    def one(i):
+        q, qp, kn = reqs[i]
+        return orc.cpu_sparse_request(q, qp, K, V, zTs[i], wq, wk, kn, lg["lo"], lg["hi"], lg["k"], L, 1 / math.sqrt(D))
+
+    with threadpool_limits(1), ThreadPoolExecutor(workers) as ex:
+        list(ex.map(one, range(workers)))                       # warm-up
+        rounds, t0 = 0, time.perf_counter()
+        while True:
+            list(ex.map(one, range(workers)))
+            rounds += 1
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        wall = time.perf_counter() - t0
+    per_round = wall / rounds                                   # `workers` requests of one layer
+    step_s = per_round * (B / workers) * layers                 # B requests x all layers
+    return {"value": B / step_s, "unit": "tokens/s", "cores": workers, "kind": "port",
+            "sample": f"{rounds} rounds x {workers} concurrent (layer, request) steps of the workload's shape "
+                      f"(L={L}, k={lg['k']}, float32 numpy, one thread each), {wall:.1f} s wall; "
+                      f"tokens/s = B / (layers x B/workers x round time)",
+            "ms_per_layer_request": per_round * 1e3}
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    layers, B, G, h, L, rho, desc = workload(args)
+    budget = max(2.0, min(args.cpu_seconds, 60.0))
+    cpu = cpu_sample(args, B, G, h, L, rho, layers, budget)
+    line = {"impl": "reference", "metric": metric_name(args.workload), "value": cpu["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * B / cpu["value"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic",
+            "config": config_of(args, desc, B, G, h, L, rho, layers),
+            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name(workload):
+    return "decode tokens/s of the sparse score+top-k+attend hot path (all layers, append included)"
+
+
+def config_of(args, desc, B, G, h, L, rho, layers):
+    return {"workload": desc, "layers": layers, "batch_per_gpu": B, "global_batch": B * args.gpus, "seq_len": L,
+            "kv_groups": G, "heads_per_group": h, "head_dim": D, "index_width": R, "rho": rho,
+            "kv_dtype": "bf16", "index_dtype": args.index_dtype, "parallelism": f"request-sharded x{args.gpus}",
+            "l2": "inputs larger than L2: every layer has its own cache and one fused launch reads >= 126 MB"
+                  if args.workload in ("c3", "c4") else "per-layer caches (working set per launch below L2)"}
+
+
+# ------------------------------------------------------------------------------------------------ GPU side
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    import torch
+    import torch.distributed as dist
+    import attention_lab_b200 as al
+    from attention_lab_b200 import _lib
+    from attention_lab_b200.selection import build_step_plan
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    layers, B, G, h, L, rho, desc = workload(args)
+    zb = 2 if args.index_dtype == "bf16" else 4
+    idt = torch.bfloat16 if zb == 2 else torch.float32
+    kvt = torch.bfloat16
+    lg = ledger(B, G, h, L, rho, layers, zb, 2)
+    C = L                                    # the step re-decodes position L-1: append + z column are idempotent
+    plan = build_step_plan(B, G, C, L, lg["k"], dev)
+    assert (plan.k, plan.selected_count) == (lg["k"], lg["S"])
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def rnd(*shape, dtype, scale=1.0):
+        t = torch.empty(shape, dtype=dtype, device=dev)
+        t.normal_(0.0, scale, generator=gen)
+        return t
+
+    # per-layer caches, weights and step inputs, resident before timing
+    Ks = [rnd(B, G, C, D, dtype=kvt) for _ in range(layers)]
+    Vs = [rnd(B, G, C, D, dtype=kvt) for _ in range(layers)]
+    Zs = [rnd(B, G, R, C, dtype=idt, scale=0.23) for _ in range(layers)]
+    WQ = [rnd(G, h * D, R, dtype=idt, scale=0.02 / math.sqrt(R)) for _ in range(layers)]
+    WK = [rnd(G, R, D, dtype=idt, scale=0.02) for _ in range(layers)]
+    Q = [rnd(B, G, h, 1, D, dtype=kvt) for _ in range(layers)]
+    QP = [rnd(B, G, h, 1, D, dtype=idt) for _ in range(layers)]
+    KPN = [rnd(B, G, 1, D, dtype=idt) for _ in range(layers)]
+    KN = [rnd(B, G, 1, D, dtype=kvt) for _ in range(layers)]
+    VN = [rnd(B, G, 1, D, dtype=kvt) for _ in range(layers)]
+    OUT = [torch.empty(B, G, h, 1, D, dtype=kvt, device=dev) for _ in range(layers)]
+    lib = _lib.load()
+    idx_code = _lib.AL_BF16 if zb == 2 else _lib.AL_F32
+    kv_strides = (_lib.strides(KN[0], 4), _lib.strides(VN[0], 4))
+    scale = 1 / math.sqrt(D)
+
+    def append_args(l, stream):
+        return (Ks[l].data_ptr(), Vs[l].data_ptr(), _lib.AL_BF16, KN[l].data_ptr(), kv_strides[0], VN[l].data_ptr(),
+                kv_strides[1], _lib.AL_BF16, None, 0, None, None, None, None, None, B, G, C, D, R, L - 1, 1, stream)
+
+    def step_args(l, stream):
+        return (Q[l].data_ptr(), Q[l].stride(0), Q[l].stride(1), Q[l].stride(2),
+                QP[l].data_ptr(), QP[l].stride(0), QP[l].stride(1), QP[l].stride(2),
+                Ks[l].data_ptr(), Vs[l].data_ptr(), _lib.AL_BF16, Zs[l].data_ptr(), WQ[l].data_ptr(),
+                WK[l].data_ptr(), idx_code, KPN[l].data_ptr(), KPN[l].stride(0), KPN[l].stride(1),
+                plan.fixed_rows.data_ptr(), plan.off_lo.data_ptr(), B, G, h, D, R, C, plan.lo, plan.hi, plan.k,
+                plan.selected_count, plan.fixed_count, plan.write_col, scale, 0, OUT[l].data_ptr(), None, None,
+                args.cluster, stream)
+
+    stream = torch.cuda.Stream(device=dev)
+    sh = stream.cuda_stream
+    A_ARGS = [append_args(l, sh) for l in range(layers)]
+    S_ARGS = [step_args(l, sh) for l in range(layers)]
+
+    def step_raw():
+        for l in range(layers):
+            _lib.check(lib.al_append_kvz(*A_ARGS[l]))
+            _lib.check(lib.al_sparse_decode_step(*S_ARGS[l]))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- correctness guard before timing: one step, kernel error word clear
+    with torch.cuda.stream(stream):
+        step_raw()
+    torch.cuda.synchronize(dev)
+    assert _lib.device_status() == 0
+
+    # ---- capture one step (2 launches per layer) as a CUDA graph
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step_raw()
+    torch.cuda.synchronize(dev)
+
+    # ---- device-timed value: K graph replays after W warm-ups
+    for _ in range(max(3, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    torch.cuda.synchronize(dev)
+    t_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    value = world * B / (t_ms / 1e3)
+
+    # ---- roofline of the dominant kernel: each fused launch timed on its own stream with events
+    n_roof = min(args.steps, 10)
+    starts = [[torch.cuda.Event(enable_timing=True) for _ in range(layers)] for _ in range(n_roof)]
+    ends = [[torch.cuda.Event(enable_timing=True) for _ in range(layers)] for _ in range(n_roof)]
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(n_roof):
+            for l in range(layers):
+                starts[i][l].record(stream)
+                _lib.check(lib.al_sparse_decode_step(*S_ARGS[l]))
+                ends[i][l].record(stream)
+        a0.record(stream)
+        for i in range(n_roof):
+            for l in range(layers):
+                _lib.check(lib.al_append_kvz(*A_ARGS[l]))
+        a1.record(stream)
+    torch.cuda.synchronize(dev)
+    durs = [starts[i][l].elapsed_time(ends[i][l]) for i in range(n_roof) for l in range(layers)]
+    fused_ms = max_over_ranks(statistics.mean(durs))
+    append_ms = a0.elapsed_time(a1) / (n_roof * layers)
+    peak, peak_src = measured_peak()
+    achieved = lg["per_launch"] / (fused_ms / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": None,
+                "kernel": "sparse_step_kernel (fused z column + u + scan + radix top-k + gather-free attend)",
+                "bytes_per_launch": lg["per_launch"], "launch_ms": round(fused_ms, 5), "peak_source": peak_src,
+                "bytes_rule": "B x (G*r*M*zb + S*G*d*2*eb) per launch (scripts/roofline.py:61-74 terms)"}
+    traffic_file = ROOT / "profiles" / f"traffic_{args.workload}_{args.index_dtype}.json"
+    if traffic_file.exists():
+        try:
+            roofline["traffic"] = json.loads(traffic_file.read_text()).get("dram_bytes_per_launch")
+        except ValueError:
+            pass
+
+    # ---- e2e through the public API with host buffers: H2D of every layer's step inputs, the drop-in operators,
+    #      D2H of every layer's attention output
+    e2e = None
+    if not args.no_e2e:
+        host_in = [[t.cpu().pin_memory() for t in (Q[l], QP[l], KPN[l], KN[l], VN[l])] for l in range(layers)]
+        host_out = [torch.empty(OUT[0].shape, dtype=kvt).pin_memory() for _ in range(layers)]
+        dev_in = [[torch.empty_like(t) for t in (Q[l], QP[l], KPN[l], KN[l], VN[l])] for l in range(layers)]
+        h2d = sum(t.numel() * t.element_size() for row in host_in for t in row)
+        d2h = sum(t.numel() * t.element_size() for t in host_out)
+
+        def e2e_step():
+            for l in range(layers):
+                for dst, src in zip(dev_in[l], host_in[l]):
+                    dst.copy_(src, non_blocking=True)
+            for l in range(layers):
+                q, qp, kpn, kn, vn = dev_in[l]
+                al.append_kvz(Ks[l], Vs[l], None, L - 1, kn, vn)
+                out = al.sparse_decode_step_kernel(q, qp, Ks[l], Vs[l], Zs[l], WQ[l], WK[l], plan.fixed_rows,
+                                                   plan.off_lo, plan.lo, plan.hi, plan.k, plan.selected_count,
+                                                   k_pre_new=kpn, write_col=plan.write_col, scale=scale,
+                                                   cluster=args.cluster)
+                host_out[l].copy_(out, non_blocking=True)
+
+        n_e2e = max(3, min(args.steps, 30))
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                e2e_step()
+            torch.cuda.synchronize(dev)
+            barrier()
+            torch.cuda.synchronize(dev)
+            f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            f0.record(stream)
+            for _ in range(n_e2e):
+                e2e_step()
+            f1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / n_e2e
+        e2e = {"value": world * B / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4), "steps": n_e2e,
+               "path": "attention_lab_b200.append_kvz + sparse_decode_step_kernel per layer, pinned host I/O"}
+
+    # ---- same-box baselines (rank 0 reports its own): dense decode over the same caches
+    baselines = None
+    if not args.no_baselines and rank == 0:
+        baselines = same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(args, B, G, h, L, rho, layers, args.cpu_seconds)
+        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    if rank == 0:
+        line = {"metric": metric_name(args.workload), "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": config_of(args, desc, B, G, h, L, rho, layers),
+                "score_attend_us_per_layer": round(fused_ms * 1e3, 2), "append_us_per_layer": round(append_ms * 1e3, 2),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": 2 * layers * args.steps,
+                "clocks": clocks.summary(), "same_box": baselines}
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale):
+    """Dense decode over the same 36-layer caches: torch SDPA with the h heads folded into the query axis (the
+    reference's full_attention(backend="sdpa_fold"), full.py:31-34) and this library's own dense kernel."""
+    import torch.nn.functional as F
+    out = {}
+
+    def timed(fn, n=5):
+        with torch.cuda.stream(stream):
+            for _ in range(2):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(n):
+                fn()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    def sdpa_fold():
+        for l in range(layers):
+            q = Q[l]
+            b, g, h, _, d = q.shape
+            F.scaled_dot_product_attention(q.view(b, g, h, d), Ks[l], Vs[l], scale=scale)
+
+    def ours_dense():
+        for l in range(layers):
+            al.dense_decode_step(Q[l], Ks[l], Vs[l], L, scale=scale)
+
+    try:
+        ms = timed(sdpa_fold)
+        out["torch_sdpa_fold_dense"] = {"tokens_per_s": round(B / (ms / 1e3), 2), "ms_per_step": round(ms, 3)}
+    except RuntimeError as e:
+        out["torch_sdpa_fold_dense"] = {"error": str(e)[:200]}
+    ms = timed(ours_dense)
+    out["ours_dense"] = {"tokens_per_s": round(B / (ms / 1e3), 2), "ms_per_step": round(ms, 3)}
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -387,3 +387,28 @@ def layer_request_bytes(*, G: int, d: int, r: int, M: int, S: int, zb: int, eb: 
     score = G * r * M * zb
     attend = S * G * d * 2 * eb
     return {"score_bytes": score, "attend_bytes": attend, "d_s1_bytes": score + attend}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# float32 CPU decode step for timing (the reference's own device-agnostic torch path, decode.py:145-163, runs the
+# same arithmetic on CPU in float32); used only as the measured CPU baseline
+# ---------------------------------------------------------------------------------------------------------------------
+def cpu_sparse_request(q, q_pre, K, V, zT, wq_t, wk, k_new, lo: int, hi: int, k: int, L: int, scale: float):
+    """One (layer, request) step in float32 on CPU. q, q_pre [G,h,d]; K, V [G,C,d]; zT [G,r,C]; wq_t [G,h*d,r];
+    wk [G,r,d]; k_new [G,d]. Writes z of the newest key into zT[:, :, L-1]; returns out [G,h,d]."""
+    G, h, d = q.shape
+    zT[:, :, L - 1] = np.einsum("gjd,gd->gj", wk, k_new)                              # decode.py:156-157
+    u = np.einsum("gf,gfj->gj", q_pre.reshape(G, h * d), wq_t)                         # indexer.py:20-24
+    out = np.empty((G, h, d), dtype=np.float32)
+    fixed = np.r_[0:lo, hi:L]
+    for g in range(G):
+        s = u[g] @ zT[g, :, lo:hi]                                                      # indexer.py:27-29
+        top = np.argpartition(-s, k - 1)[:k] + lo if 0 < k < s.shape[0] else np.arange(lo, lo + k)   # decode.py:92
+        rows = np.concatenate([fixed, top])
+        ks, vs = K[g, rows], V[g, rows]                                                 # decode.py:140-141
+        sc = (q[g] @ ks.T) * scale                                                      # sparse.py:40-60
+        sc -= sc.max(axis=1, keepdims=True)
+        p = np.exp(sc)
+        p /= p.sum(axis=1, keepdims=True)
+        out[g] = p @ vs
+    return out

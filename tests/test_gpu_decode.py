@@ -151,7 +151,8 @@ def test_dense_decode_matches_reference(name):
         n = cs.to_np
         want = orc.dense_decode_step(n(g["q"].cpu()), n(g["k"].cpu()), n(g["v"].cpu()), case.L, 1 / math.sqrt(case.d))
         check_out(out.float().cpu().numpy(), want, case.kv_dtype, f"dense cluster {cl}")
-        check_out(out.float().cpu().numpy(), gd["dense"], case.kv_dtype, "dense vs reference")
+        ref_kind = "float32" if case.kv_dtype == "float32" else "bfloat16_vs_bfloat16"
+        check_out(out.float().cpu().numpy(), gd["dense"], ref_kind, "dense vs reference")
 
 
 def test_full_selection_equals_dense():
