@@ -1,12 +1,17 @@
 // Gather-free attention engine: one CTA attends its h query heads over a list of K/V rows read in place.
 //
 // Rows are flat ids into the flattened [B*G*C, d] cache (the reference's row-id convention, sparse.py:14-16).
-// The engine streams the listed rows through shared memory with a 4-stage cp.async pipeline (16-byte chunks, a
-// row is 16 threads x 16 B for bf16), in two sweeps per chunk of rows: a K sweep that scores every row for all h
-// heads and keeps the scores in shared memory, then a V sweep that accumulates p * v with the chunk's exact maximum,
-// so no per-row rescale is needed (one rescale per chunk of up to 1024 rows). Lane layout: 8 lanes per row, 16 dims
-// per lane; the 8 lanes of a row reduce a dot product with 3 xor-shuffles. The result is the CTA's unnormalised
-// partial (m, l, acc) per head in the log2 domain, merged across a thread-block cluster by `finish_output`.
+// The engine streams the listed rows through shared memory with a multi-stage cp.async pipeline (16-byte chunks, a
+// bf16 row is 16 threads x 16 B; 4 to 8 stages of 64 rows, as shared memory allows), in three steps per chunk of up
+// to 1024 rows. (One-dimensional bulk copies, one per 256-byte row, measured about 2.5x slower on B200: the copy
+// engine's per-request cost dominates at this row size.)
+//   K sweep  - 16 lanes per row, 8 dims per lane; the h partial dot products are reduced across the 16 lanes with a
+//              transposed butterfly (5 shuffles for 4 heads) and the scores stored in shared memory;
+//   p pass   - the chunk's exact per-head maximum rescales the running state once, then p = exp2(s - m) is computed
+//              once per (row, head) in place and summed into l;
+//   V sweep  - acc += p * v with the same 16-lane layout.
+// No per-row rescale is needed. The result is the CTA's unnormalised partial (m, l, acc) per head in the log2
+// domain, merged across a thread-block cluster by `finish_output`.
 #pragma once
 #include "al_common.cuh"
 
@@ -15,19 +20,24 @@ namespace al {
 template <typename KV_T, int HP>
 struct AttendCfg {
   static constexpr int VE = V16<KV_T>::n;                 // elements per 16-byte chunk
-  static constexpr int NCH = kHeadDim / VE;               // chunks per row
-  static constexpr int NCL = NCH / 8;                     // chunks per lane
+  static constexpr int NCH = kHeadDim / VE;               // chunks per row (16 bf16, 32 fp32)
+  static constexpr int NCL = NCH / 16;                    // chunks per lane (1 bf16, 2 fp32)
+  static constexpr int DPL = 8;                           // dims per lane
   static constexpr int ROWB = kHeadDim * (int)sizeof(KV_T);
   static constexpr int TR = (sizeof(KV_T) == 2) ? 64 : 32;  // rows per pipeline tile
-  static constexpr int NSTAGE = 4;
-  static constexpr int RPG = TR / 32;                     // rows per 8-lane group per tile
+  static constexpr int MIN_STAGES = 4;                    // pipeline depth is a runtime value in [4, MAX_STAGES]
+  static constexpr int MAX_STAGES = 8;
+  static constexpr int LG = kThreads / 16;                // 16-lane row groups per CTA
+  static constexpr int RPG = TR / LG;                     // rows per row group per tile
   static constexpr int CHUNK = 1024;                      // rows scored before their V sweep
   static constexpr int STAGE_BYTES = TR * ROWB;
-  static constexpr int STAGES_BYTES = NSTAGE * STAGE_BYTES;
-  static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4 + kWarps * HP * 4;
-  static_assert(RED_BYTES <= STAGES_BYTES, "warp reduction buffer aliases the stage buffers");
-  // shared memory of the engine: stage buffers | chunk scores | warp maxima
-  static constexpr int SMEM = STAGES_BYTES + CHUNK * HP * 4 + kWarps * HP * 4;
+  static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4;
+  static_assert(RED_BYTES <= MIN_STAGES * STAGE_BYTES, "warp reduction buffer aliases the stage buffers");
+  static_assert(RPG >= 1 && TR % LG == 0, "tile rows must be a multiple of the row groups");
+  // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | warp maxima and sums
+  static constexpr int TAIL = CHUNK * HP * 4 + 2 * kWarps * HP * 4;
+  static constexpr __host__ __device__ int smem(int stages) { return stages * STAGE_BYTES + TAIL; }
+  static constexpr int SMEM = MIN_STAGES * STAGE_BYTES + TAIL;
 };
 
 // Row source: an explicit list in shared memory (0xffffffff marks a skipped row) or a contiguous range.
@@ -37,11 +47,17 @@ struct RowSrc {
   __device__ __forceinline__ uint32_t get(int i) const { return list ? list[i] : base + (uint32_t)i; }
 };
 
+// Every thread copies the same 16-byte chunk (tid % NCH) of rows tid / NCH + j * (kThreads / NCH) of the tile
+// [row0, row0 + TR), for the rows below n that are not skipped.
 template <typename Cfg>
 __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cache, RowSrc rows, int row0, int n,
                                            unsigned char* buf) {
-  for (int ci = threadIdx.x; ci < Cfg::TR * Cfg::NCH; ci += kThreads) {
-    const int rr = ci / Cfg::NCH, ch = ci % Cfg::NCH;
+  constexpr int CPT = Cfg::TR * Cfg::NCH / kThreads;      // chunks per thread per tile
+  constexpr int RSTEP = kThreads / Cfg::NCH;              // rows between a thread's chunks
+  const int ch = threadIdx.x % Cfg::NCH, r0 = threadIdx.x / Cfg::NCH;
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int rr = r0 + j * RSTEP;
     const int row = row0 + rr;
     if (row < n) {
       const uint32_t id = rows.get(row);
@@ -51,42 +67,98 @@ __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cac
   }
 }
 
-// Load this lane's 16 dims of row `rr` of a staged tile into floats.
+// This lane's 8 dims of row `rr` of a staged tile (chunk li, and li + 16 for fp32) as 4 float pairs.
 template <typename KV_T, typename Cfg>
-__device__ __forceinline__ void load_row(const unsigned char* buf, int rr, int li, float (&f)[16]) {
+__device__ __forceinline__ void load_row2(const unsigned char* buf, int rr, int li, float2 (&f)[4]) {
 #pragma unroll
   for (int c = 0; c < Cfg::NCL; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * Cfg::ROWB + (li + 8 * c) * 16);
-    unpack(v, f + c * Cfg::VE, (const KV_T*)nullptr);
+    const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * Cfg::ROWB + (li + 16 * c) * 16);
+    if (sizeof(KV_T) == 2) {
+      f[0] = make_float2(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u));
+      f[1] = make_float2(__uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+      f[2] = make_float2(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u));
+      f[3] = make_float2(__uint_as_float(v.w << 16), __uint_as_float(v.w & 0xffff0000u));
+    } else {
+      f[2 * c] = make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+      f[2 * c + 1] = make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
+    }
   }
 }
 
-// Dims held by lane li in slot e (0..15): chunk (li + 8*(e / VE)), element e % VE.
+// Dim held by lane li in slot e (0..7).
 template <typename Cfg>
 __device__ __forceinline__ int lane_dim(int li, int e) {
-  return (li + 8 * (e / Cfg::VE)) * Cfg::VE + (e % Cfg::VE);
+  return (li + 16 * (e / Cfg::VE)) * Cfg::VE + (e % Cfg::VE);
 }
 
-// Attend over rows[0, n_rows). q: this lane's dims, pre-multiplied by scale * log2(e). Writes the CTA partial
-// (s_m[h], s_l[h], s_acc[h][128]) to shared memory; ends with a __syncthreads().
+// Head whose full 16-lane sum lane li holds after the transposed reduction (see reduce16).
+template <int HP>
+__device__ __forceinline__ int lane_head(int li) {
+  if (HP == 4) return ((li >> 3) & 1) * 2 + ((li >> 2) & 1);
+  if (HP == 2) return (li >> 3) & 1;
+  return 0;
+}
+
+// Sum HP partial values over the 16 lanes of a row group. Lane li ends with the total of head lane_head<HP>(li).
+template <int HP>
+__device__ __forceinline__ float reduce16(const float (&v)[HP], int li) {
+  if (HP == 4) {
+    const bool b3 = (li >> 3) & 1, b2 = (li >> 2) & 1;
+    float a0 = b3 ? v[2] : v[0], a1 = b3 ? v[3] : v[1];
+    const float s0 = b3 ? v[0] : v[2], s1 = b3 ? v[1] : v[3];
+    a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
+    a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
+    float b = b2 ? a1 : a0;
+    b += __shfl_xor_sync(0xffffffffu, b2 ? a0 : a1, 4);
+    b += __shfl_xor_sync(0xffffffffu, b, 2);
+    b += __shfl_xor_sync(0xffffffffu, b, 1);
+    return b;
+  } else if (HP == 2) {
+    const bool b3 = (li >> 3) & 1;
+    float a = b3 ? v[1] : v[0];
+    a += __shfl_xor_sync(0xffffffffu, b3 ? v[0] : v[1], 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 4);
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    return a;
+  } else {
+    float a = v[0];
+    a += __shfl_xor_sync(0xffffffffu, a, 8);
+    a += __shfl_xor_sync(0xffffffffu, a, 4);
+    a += __shfl_xor_sync(0xffffffffu, a, 2);
+    a += __shfl_xor_sync(0xffffffffu, a, 1);
+    return a;
+  }
+}
+
+// Attend over rows[0, n_rows). q: this lane's 8 dims as 4 pairs, pre-multiplied by scale * log2(e). Writes the CTA
+// partial (s_m[HP], s_l[HP], s_acc[HP][128]) to shared memory; ends with a __syncthreads(). Dot products and the
+// p * v accumulation use Blackwell's paired fp32 FMA (two lanes of fp32 per instruction).
 template <typename KV_T, int HP>
 __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict__ Vf, RowSrc rows, int n_rows,
-                            const float (&q)[HP][16], unsigned char* dsm, float* s_m, float* s_l, float* s_acc) {
+                            const float2 (&q)[HP][4], unsigned char* dsm, int nstage, float* s_m, float* s_l,
+                            float* s_acc, unsigned* err) {
   using Cfg = AttendCfg<KV_T, HP>;
-  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, lg = lane >> 3, li = lane & 7;
+  (void)err;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, li = lane & 15;
+  const int grp = tid >> 4;                              // row group 0..LG-1
   unsigned char* stages = dsm;
-  float* s_sc = reinterpret_cast<float*>(dsm + Cfg::STAGES_BYTES);
-  float* s_wm = s_sc + Cfg::CHUNK * HP;
+  float* s_sc = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES);
+  float* s_wm = s_sc + Cfg::CHUNK * HP;                  // [kWarps][HP] warp maxima
+  float* s_wl = s_wm + kWarps * HP;                      // [kWarps][HP] warp sums of p
   const unsigned char* Kb = reinterpret_cast<const unsigned char*>(Kf);
   const unsigned char* Vb = reinterpret_cast<const unsigned char*>(Vf);
+  const int my_head = lane_head<HP>(li);
+  const bool head_writer = (li & (16 / HP - 1)) == 0;   // one lane per head in each row group
 
-  float m_run[HP], l_run[HP], acc[HP][16];
+  float m_run[HP], l_run[HP];
+  float2 acc[HP][4];
 #pragma unroll
   for (int hh = 0; hh < HP; ++hh) {
     m_run[hh] = -INFINITY;
     l_run[hh] = 0.f;
 #pragma unroll
-    for (int e = 0; e < 16; ++e) acc[hh][e] = 0.f;
+    for (int i = 0; i < 4; ++i) acc[hh][i] = make_float2(0.f, 0.f);
   }
 
   for (int c0 = 0; c0 < n_rows; c0 += Cfg::CHUNK) {
@@ -94,73 +166,55 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
     RowSrc rs = rows;
     if (rs.list) rs.list += c0; else rs.base += (uint32_t)c0;
     const int ntiles = (n + Cfg::TR - 1) / Cfg::TR;
-    float m_loc[HP];
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) m_loc[hh] = -INFINITY;
+    float m_loc = -INFINITY;                            // max of this lane's head over its rows
 
-    // ---------------- K sweep: scores of every row of the chunk ----------------
-#pragma unroll
-    for (int s = 0; s < Cfg::NSTAGE - 1; ++s) {
+    // ---------------- K sweep ----------------
+    for (int s = 0; s < nstage - 1; ++s) {
       if (s < ntiles) issue_tile<Cfg>(Kb, rs, s * Cfg::TR, n, stages + s * Cfg::STAGE_BYTES);
       cp_async_commit();
     }
+    int scur = 0, snext = nstage - 1;                   // stage of tile t, stage the next issue fills
     for (int t = 0; t < ntiles; ++t) {
-      cp_async_wait<Cfg::NSTAGE - 2>();
-      __syncthreads();
-      const int tn = t + Cfg::NSTAGE - 1;
-      if (tn < ntiles) issue_tile<Cfg>(Kb, rs, tn * Cfg::TR, n, stages + (tn % Cfg::NSTAGE) * Cfg::STAGE_BYTES);
+      cp_async_wait_dyn(nstage - 2);
+      __syncthreads();                                  // tile t landed for everyone; tile t-1's stage is free
+      const int tn = t + nstage - 1;
+      if (tn < ntiles) issue_tile<Cfg>(Kb, rs, tn * Cfg::TR, n, stages + snext * Cfg::STAGE_BYTES);
       cp_async_commit();
-      const unsigned char* buf = stages + (t % Cfg::NSTAGE) * Cfg::STAGE_BYTES;
+      const unsigned char* buf = stages + scur * Cfg::STAGE_BYTES;
+      scur = scur + 1 == nstage ? 0 : scur + 1;
+      snext = snext + 1 == nstage ? 0 : snext + 1;
 #pragma unroll
       for (int i = 0; i < Cfg::RPG; ++i) {
-        const int rr = (w * 4 + lg) * Cfg::RPG + i;
+        const int rr = grp * Cfg::RPG + i;
         const int row = t * Cfg::TR + rr;
         const bool valid = row < n && rs.get(row) != 0xffffffffu;
-        float kf[16];
-        if (valid) load_row<KV_T, Cfg>(buf, rr, li, kf);
+        float2 kf[4];
+        if (valid) load_row2<KV_T, Cfg>(buf, rr, li, kf);
         else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e) kf[e] = 0.f;
+          for (int e = 0; e < 4; ++e) kf[e] = make_float2(0.f, 0.f);
         }
-        float sc[HP];
+        float part[HP];
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh) {
-          float a = 0.f;
-#pragma unroll
-          for (int e = 0; e < 16; ++e) a = fmaf(q[hh][e], kf[e], a);
-          sc[hh] = a;
+          float2 a = __fmul2_rn(q[hh][0], kf[0]);
+          a = __ffma2_rn(q[hh][1], kf[1], a);
+          a = __ffma2_rn(q[hh][2], kf[2], a);
+          a = __ffma2_rn(q[hh][3], kf[3], a);
+          part[hh] = a.x + a.y;
         }
-#pragma unroll
-        for (int hh = 0; hh < HP; ++hh) {
-          sc[hh] += __shfl_xor_sync(0xffffffffu, sc[hh], 1);
-          sc[hh] += __shfl_xor_sync(0xffffffffu, sc[hh], 2);
-          sc[hh] += __shfl_xor_sync(0xffffffffu, sc[hh], 4);
-          if (!valid) sc[hh] = -INFINITY;
-          m_loc[hh] = fmaxf(m_loc[hh], sc[hh]);
-        }
-        if (row < n && li < HP) {
-          float v = sc[0];
-#pragma unroll
-          for (int hh = 1; hh < HP; ++hh) v = (li == hh) ? sc[hh] : v;
-          s_sc[row * HP + li] = v;
-        }
+        float sc = reduce16<HP>(part, li);
+        if (!valid) sc = -INFINITY;
+        m_loc = fmaxf(m_loc, sc);
+        if (row < n && head_writer) s_sc[row * HP + my_head] = sc;
       }
     }
     cp_async_wait<0>();
 
-    // chunk maximum per head, then one rescale of the running state
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) {
-      m_loc[hh] = fmaxf(m_loc[hh], __shfl_xor_sync(0xffffffffu, m_loc[hh], 8));
-      m_loc[hh] = fmaxf(m_loc[hh], __shfl_xor_sync(0xffffffffu, m_loc[hh], 16));
-    }
-    if (lane < HP) {
-      float v = m_loc[0];
-#pragma unroll
-      for (int hh = 1; hh < HP; ++hh) v = (lane == hh) ? m_loc[hh] : v;
-      s_wm[w * HP + lane] = v;
-    }
-    __syncthreads();   // scores, warp maxima visible; every thread is done with the K tiles
+    // ---------------- chunk maximum, one rescale, p = exp2(s - m) in place ----------------
+    m_loc = fmaxf(m_loc, __shfl_xor_sync(0xffffffffu, m_loc, 16));   // the other row group of the warp
+    if (lane < 16 && head_writer) s_wm[w * HP + my_head] = m_loc;
+    __syncthreads();                                    // scores + warp maxima visible; K tiles consumed
 #pragma unroll
     for (int hh = 0; hh < HP; ++hh) {
       float mc = -INFINITY;
@@ -170,72 +224,104 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
       const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run[hh] - mn);
       m_run[hh] = mn;
       l_run[hh] *= corr;
+      const float2 c2 = make_float2(corr, corr);
 #pragma unroll
-      for (int e = 0; e < 16; ++e) acc[hh][e] *= corr;
+      for (int i = 0; i < 4; ++i) acc[hh][i] = __fmul2_rn(acc[hh][i], c2);
     }
-
-    // ---------------- V sweep: acc += exp2(s - m) * v ----------------
-#pragma unroll
-    for (int s = 0; s < Cfg::NSTAGE - 1; ++s) {
+    // V prologue first, so the loads overlap the exp pass
+    for (int s = 0; s < nstage - 1; ++s) {
       if (s < ntiles) issue_tile<Cfg>(Vb, rs, s * Cfg::TR, n, stages + s * Cfg::STAGE_BYTES);
       cp_async_commit();
     }
+    float psum[HP];
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) psum[hh] = 0.f;
+    for (int i = tid; i < n * HP; i += kThreads) {
+      const int hh = i % HP;
+      float mv = m_run[0];
+#pragma unroll
+      for (int x = 1; x < HP; ++x) mv = (hh == x) ? m_run[x] : mv;
+      const float sv = s_sc[i];
+      const float pv = (mv == -INFINITY || sv == -INFINITY) ? 0.f : exp2f(sv - mv);
+      s_sc[i] = pv;
+#pragma unroll
+      for (int x = 0; x < HP; ++x) psum[x] += (hh == x) ? pv : 0.f;
+    }
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) psum[hh] += __shfl_xor_sync(0xffffffffu, psum[hh], o);
+    }
+    if (lane == 0) {
+#pragma unroll
+      for (int hh = 0; hh < HP; ++hh) s_wl[w * HP + hh] = psum[hh];
+    }
+    __syncthreads();                                    // p and the sums visible
+#pragma unroll
+    for (int hh = 0; hh < HP; ++hh) {
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) sum += s_wl[i * HP + hh];
+      l_run[hh] += sum;
+    }
+
+    // ---------------- V sweep: acc += p * v ----------------
+    scur = 0;
+    snext = nstage - 1;
     for (int t = 0; t < ntiles; ++t) {
-      cp_async_wait<Cfg::NSTAGE - 2>();
+      cp_async_wait_dyn(nstage - 2);
       __syncthreads();
-      const int tn = t + Cfg::NSTAGE - 1;
-      if (tn < ntiles) issue_tile<Cfg>(Vb, rs, tn * Cfg::TR, n, stages + (tn % Cfg::NSTAGE) * Cfg::STAGE_BYTES);
+      const int tn = t + nstage - 1;
+      if (tn < ntiles) issue_tile<Cfg>(Vb, rs, tn * Cfg::TR, n, stages + snext * Cfg::STAGE_BYTES);
       cp_async_commit();
-      const unsigned char* buf = stages + (t % Cfg::NSTAGE) * Cfg::STAGE_BYTES;
+      const unsigned char* buf = stages + scur * Cfg::STAGE_BYTES;
+      scur = scur + 1 == nstage ? 0 : scur + 1;
+      snext = snext + 1 == nstage ? 0 : snext + 1;
 #pragma unroll
       for (int i = 0; i < Cfg::RPG; ++i) {
-        const int rr = (w * 4 + lg) * Cfg::RPG + i;
+        const int rr = grp * Cfg::RPG + i;
         const int row = t * Cfg::TR + rr;
         if (row < n && rs.get(row) != 0xffffffffu) {
           float p[HP];
+          if (HP == 4) {
+            const float4 p4 = *reinterpret_cast<const float4*>(s_sc + row * HP);
+            p[0] = p4.x; p[1 % HP] = p4.y; p[2 % HP] = p4.z; p[3 % HP] = p4.w;
+          } else {
+#pragma unroll
+            for (int hh = 0; hh < HP; ++hh) p[hh] = s_sc[row * HP + hh];
+          }
+          float2 vf[4];
+          load_row2<KV_T, Cfg>(buf, rr, li, vf);
 #pragma unroll
           for (int hh = 0; hh < HP; ++hh) {
-            const float sv = s_sc[row * HP + hh];
-            p[hh] = (m_run[hh] == -INFINITY) ? 0.f : exp2f(sv - m_run[hh]);
-            l_run[hh] += p[hh];
+            const float2 p2 = make_float2(p[hh], p[hh]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[hh][e] = __ffma2_rn(p2, vf[e], acc[hh][e]);
           }
-          float vf[16];
-          load_row<KV_T, Cfg>(buf, rr, li, vf);
-#pragma unroll
-          for (int hh = 0; hh < HP; ++hh)
-#pragma unroll
-            for (int e = 0; e < 16; ++e) acc[hh][e] = fmaf(p[hh], vf[e], acc[hh][e]);
         }
       }
     }
     cp_async_wait<0>();
-    __syncthreads();   // V tiles consumed; the next chunk (or the reduction) may reuse the stage buffers
+    __syncthreads();   // V tiles and p consumed; the next chunk (or the reduction) may reuse the buffers
   }
 
-  // ---------------- CTA reduction: 4 row groups per warp, then 8 warps ----------------
+  // ---------------- CTA reduction: 2 row groups per warp, then the warps ----------------
 #pragma unroll
-  for (int hh = 0; hh < HP; ++hh) {
-    l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 8);
-    l_run[hh] += __shfl_xor_sync(0xffffffffu, l_run[hh], 16);
+  for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-      acc[hh][e] += __shfl_xor_sync(0xffffffffu, acc[hh][e], 8);
-      acc[hh][e] += __shfl_xor_sync(0xffffffffu, acc[hh][e], 16);
+    for (int e = 0; e < 4; ++e) {
+      acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
+      acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
     }
-  }
   float* red = reinterpret_cast<float*>(stages);           // [kWarps][HP][128]
-  float* redl = red + kWarps * HP * kHeadDim;               // [kWarps][HP]
-  if (lg == 0) {
+  if (lane < 16) {
 #pragma unroll
     for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
-      for (int e = 0; e < 16; ++e) red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, e)] = acc[hh][e];
-    if (li < HP) {
-      float v = l_run[0];
-#pragma unroll
-      for (int hh = 1; hh < HP; ++hh) v = (li == hh) ? l_run[hh] : v;
-      redl[w * HP + li] = v;
-    }
+      for (int e = 0; e < 4; ++e) {
+        red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e)] = acc[hh][e].x;
+        red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e + 1)] = acc[hh][e].y;
+      }
   }
   __syncthreads();
   for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) {
@@ -245,14 +331,14 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
     s_acc[idx] = a;
   }
   if (tid < HP) {
-    float l = 0.f;
+    float mv = m_run[0], lv = l_run[0];
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) l += redl[i * HP + tid];
-    s_l[tid] = l;
-    float mv = m_run[0];
-#pragma unroll
-    for (int hh = 1; hh < HP; ++hh) mv = (tid == hh) ? m_run[hh] : mv;
+    for (int hh = 1; hh < HP; ++hh) {
+      mv = (tid == hh) ? m_run[hh] : mv;
+      lv = (tid == hh) ? l_run[hh] : lv;
+    }
     s_m[tid] = mv;
+    s_l[tid] = lv;
   }
   __syncthreads();
 }
@@ -291,17 +377,20 @@ __device__ void finish_output(KV_T* __restrict__ out, float* __restrict__ part, 
   if (CS > 1) cluster.sync();   // peers keep their shared memory alive until rank 0 has read it
 }
 
-// This lane's q dims (pre-scaled by scale*log2 e) for the heads of one (batch, group).
+// This lane's q dims (pre-scaled by scale*log2 e) for the heads of one (batch, group), as 4 pairs per head.
 template <typename KV_T, int HP>
 __device__ __forceinline__ void load_q(const KV_T* __restrict__ qb, long long sh, int h, float scale_log2,
-                                       float (&q)[HP][16]) {
+                                       float2 (&q)[HP][4]) {
   using Cfg = AttendCfg<KV_T, HP>;
-  const int li = threadIdx.x & 7;
+  const int li = threadIdx.x & 15;
 #pragma unroll
   for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
-    for (int e = 0; e < 16; ++e)
-      q[hh][e] = (hh < h) ? tof(qb[hh * sh + lane_dim<Cfg>(li, e)]) * scale_log2 : 0.f;
+    for (int e = 0; e < 4; ++e) {
+      const float x = (hh < h) ? tof(qb[hh * sh + lane_dim<Cfg>(li, 2 * e)]) * scale_log2 : 0.f;
+      const float y = (hh < h) ? tof(qb[hh * sh + lane_dim<Cfg>(li, 2 * e + 1)]) * scale_log2 : 0.f;
+      q[hh][e] = make_float2(x, y);
+    }
 }
 
 }  // namespace al

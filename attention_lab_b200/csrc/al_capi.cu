@@ -3,6 +3,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <mutex>
 #include <unordered_map>
 
@@ -137,17 +138,19 @@ int pad_heads(int h) { return h <= 1 ? 1 : (h <= 2 ? 2 : 4); }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Static shared memory of the fused kernel (upper bound used for the dynamic budget).
-constexpr int kFusedStaticBytes = 24 * 1024;
+constexpr int kFusedStaticBytes = 40 * 1024;
 constexpr int kAttendStaticBytes = 4 * 1024;
 
-int engine_smem(int kv_dtype, int hp) {
+constexpr int kStages = 8;   // attend pipeline depth: registers already limit a 512-thread CTA to one per SM
+
+int engine_smem(int kv_dtype, int hp, int stages = kStages) {
   switch (kv_dtype * 8 + hp) {
-    case AL_F32 * 8 + 1: return AttendCfg<float, 1>::SMEM;
-    case AL_F32 * 8 + 2: return AttendCfg<float, 2>::SMEM;
-    case AL_F32 * 8 + 4: return AttendCfg<float, 4>::SMEM;
-    case AL_BF16 * 8 + 1: return AttendCfg<__nv_bfloat16, 1>::SMEM;
-    case AL_BF16 * 8 + 2: return AttendCfg<__nv_bfloat16, 2>::SMEM;
-    default: return AttendCfg<__nv_bfloat16, 4>::SMEM;
+    case AL_F32 * 8 + 1: return AttendCfg<float, 1>::smem(stages);
+    case AL_F32 * 8 + 2: return AttendCfg<float, 2>::smem(stages);
+    case AL_F32 * 8 + 4: return AttendCfg<float, 4>::smem(stages);
+    case AL_BF16 * 8 + 1: return AttendCfg<__nv_bfloat16, 1>::smem(stages);
+    case AL_BF16 * 8 + 2: return AttendCfg<__nv_bfloat16, 2>::smem(stages);
+    default: return AttendCfg<__nv_bfloat16, 4>::smem(stages);
   }
 }
 
@@ -231,21 +234,34 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
   if (p.scan && !p.u_in && (!p.q_pre || !p.wq_t)) return fail(AL_EINVAL, "null q_pre or wq_t");
   const int ez = esize(idx_dtype);
   p.zvec = ((long long)p.C * ez % 16 == 0) && aligned16(p.zT) ? 1 : 0;
+  p.uvec = (p.r == kMaxR && p.wq_t && aligned16(p.wq_t)) ? 1 : 0;
 
   const int hp = attend ? pad_heads(p.h) : 1;
-  const int eng = attend ? engine_smem(kv_dtype, hp) : 0;
   const int budget = di->max_smem_optin - kFusedStaticBytes;
-  const int max_keys = (budget - 4096 - 8 * 1024) / 4;   // room left for the row list
-  int cs = cluster > 0 ? cluster : auto_cluster(p.B * p.G, p.M, di->sms, max_keys);
+  // Shared memory per CTA: [keys | candidate list] aliased with the attend engine, then the attend row list.
+  // The cluster size is the automatic (or requested) one, grown while a CTA's share does not fit.
+  int cs = cluster > 0 ? cluster : auto_cluster(p.B * p.G, p.M, di->sms, 1 << 30);
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
-  p.cpc = (int)round_up((size_t)((p.M + cs - 1) / cs), 8);
-  if (p.cpc == 0) p.cpc = 8;
-  const size_t keys_bytes = p.scan || p.select_mode != 0 ? (size_t)p.cpc * 4 : 0;
-  p.union_bytes = (int)round_up(keys_bytes > (size_t)eng ? keys_bytes : (size_t)eng, 128);
-  const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
-  const size_t smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
-  if ((long long)smem > budget)
-    return fail(AL_EUNSUPPORTED, "candidate range too large for cluster %d: %zu bytes of shared memory per CTA", cs, smem);
+  size_t smem = 0;
+  for (;; cs <<= 1) {
+    p.cpc = (int)round_up((size_t)((p.M + cs - 1) / cs), 8);
+    if (p.cpc == 0) p.cpc = 8;
+    p.keys_bytes = (p.scan || p.select_mode != 0) ? (int)round_up((size_t)(p.cpc + 24) * 4, 16) : 0;
+    p.ccap = p.select_mode == 1 ? std::min(p.cpc + 8, 2 * p.k + 1024) : 0;
+    const size_t select_bytes = (size_t)p.keys_bytes + (size_t)p.ccap * 8;
+    const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
+    bool fits = false;
+    for (int st = kStages; st >= 4 && !fits; --st) {
+      const size_t eng = attend ? (size_t)engine_smem(kv_dtype, hp, st) : 0;
+      p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
+      smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
+      p.nstage = st;
+      fits = (long long)smem <= budget;
+    }
+    if (fits) break;
+    if (cluster > 0 || cs >= kMaxCluster)
+      return fail(AL_EUNSUPPORTED, "candidate range too large for cluster %d: %zu bytes of shared memory per CTA", cs, smem);
+  }
   p.err = di->err;
   dim3 grid((unsigned)cs, (unsigned)(p.B * p.G), 1);
   if (!attend) { p.out = nullptr; p.part = nullptr; }
@@ -339,6 +355,7 @@ static int run_attend(AttendParams p, int kv_dtype, int d, int n_all, int cluste
   }
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
   p.rows_cap = p.mode == 0 ? (n_all + cs - 1) / cs : 0;
+  p.nstage = kStages;
   const size_t smem = (size_t)engine_smem(kv_dtype, hp) + (size_t)p.rows_cap * 4;
   if ((long long)smem > di->max_smem_optin - kAttendStaticBytes)
     return fail(AL_EUNSUPPORTED, "row list too long for cluster %d (%zu bytes of shared memory)", cs, smem);

@@ -298,3 +298,26 @@ def test_validation_raises_value_error():
     with pytest.raises(ValueError):
         q64 = g["q"][..., :64].contiguous()
         al.dense_decode_step(q64, g["k"][..., :64].contiguous(), g["v"][..., :64].contiguous(), 100)
+
+
+@pytest.mark.parametrize("pattern", ["all_equal", "three_values"])
+def test_ties_go_to_the_smaller_position_for_every_cluster_size(pattern):
+    """Heavy ties: index columns repeat one (or three) z vectors, so scores tie exactly. The chosen set must be the
+    oracle's (score desc, position asc) top-k for every cluster size; all-equal scores also overflow the candidate
+    list and exercise the full-array fallback."""
+    case = cs.CASES["c1"]
+    t = cs.build(case)
+    c = cs.step_constants(case)
+    zt = t["zT"]
+    if pattern == "all_equal":
+        zt[..., :case.L - 1] = zt[..., 100:101]
+    else:
+        idx = torch.arange(case.L - 1) % 3
+        zt[..., :case.L - 1] = zt[..., 100:103][..., idx]
+    n = cs.to_np
+    s64 = oracle_scores(t, c)
+    want = orc.topk_indices(s64, c["k"]) + c["lo"]
+    for cl in (1, 2, 4, 8, 16):
+        _, _, _, _, rows, _, _ = run_step(case, cluster=cl, t=t)
+        got = rows.reshape(case.B, case.G, -1)[..., c["fixed_count"]:] - c["off_lo"] + c["lo"]
+        assert np.array_equal(np.sort(got, axis=-1), np.sort(want, axis=-1)), f"cluster {cl}"
