@@ -21,23 +21,27 @@ template <typename KV_T, int HP>
 struct AttendCfg {
   static constexpr int VE = V16<KV_T>::n;                 // elements per 16-byte chunk
   static constexpr int NCH = kHeadDim / VE;               // chunks per row (16 bf16, 32 fp32)
-  static constexpr int NCL = NCH / 16;                    // chunks per lane (1 bf16, 2 fp32)
-  static constexpr int DPL = 8;                           // dims per lane
+  static constexpr int NCL = NCH / 16;                    // chunks per lane in the V sweep (1 bf16, 2 fp32)
   static constexpr int ROWB = kHeadDim * (int)sizeof(KV_T);
-  static constexpr int TR = (sizeof(KV_T) == 2) ? 64 : 32;  // rows per pipeline tile
-  static constexpr int MIN_STAGES = 4;                    // pipeline depth is a runtime value in [4, MAX_STAGES]
-  static constexpr int MAX_STAGES = 8;
-  static constexpr int LG = kThreads / 16;                // 16-lane row groups per CTA
-  static constexpr int RPG = TR / LG;                     // rows per row group per tile
-  static constexpr int CHUNK = 1024;                      // rows scored before their V sweep
+  static constexpr int TR = (sizeof(KV_T) == 2) ? 128 : 64;  // rows per pipeline tile (32 KB)
+  static constexpr int MIN_STAGES = 3;                    // pipeline depth is a runtime value in [3, MAX_STAGES]
+  static constexpr int MAX_STAGES = 5;
+  static constexpr int KPARTS = kThreads / TR;            // K sweep: threads per row (4 bf16, 8 fp32)
+  static constexpr int KCH = NCH / KPARTS;                // K sweep: chunks per thread (4)
+  static constexpr int LG = kThreads / 16;                // V sweep: 16-lane row groups per CTA
+  static constexpr int RPG = TR / LG;                     // V sweep: rows per row group per tile
+  static constexpr int CHUNK = 2048;                      // rows scored before their V sweep
   static constexpr int STAGE_BYTES = TR * ROWB;
   static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4;
   static_assert(RED_BYTES <= MIN_STAGES * STAGE_BYTES, "warp reduction buffer aliases the stage buffers");
-  static_assert(RPG >= 1 && TR % LG == 0, "tile rows must be a multiple of the row groups");
-  // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | warp maxima and sums
-  static constexpr int TAIL = CHUNK * HP * 4 + 2 * kWarps * HP * 4;
+  static_assert(RPG >= 1 && TR % LG == 0 && KCH * KPARTS == NCH && KPARTS * TR == kThreads, "tile shape");
+  // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | K partial sums |
+  // q (pre-scaled) | warp maxima and sums
+  static constexpr int TAIL = CHUNK * HP * 4 + KPARTS * TR * HP * 4 + HP * kHeadDim * 4 + 2 * kWarps * HP * 4;
   static constexpr __host__ __device__ int smem(int stages) { return stages * STAGE_BYTES + TAIL; }
   static constexpr int SMEM = MIN_STAGES * STAGE_BYTES + TAIL;
+  // a staged row holds its 16-byte chunks XOR-swizzled by the row index, so both sweeps read without bank conflicts
+  static __device__ __forceinline__ int swz(int rr, int c) { return c ^ (rr & (NCH - 1)); }
 };
 
 // Row source: an explicit list in shared memory (0xffffffff marks a skipped row) or a contiguous range.
@@ -48,7 +52,7 @@ struct RowSrc {
 };
 
 // Every thread copies the same 16-byte chunk (tid % NCH) of rows tid / NCH + j * (kThreads / NCH) of the tile
-// [row0, row0 + TR), for the rows below n that are not skipped.
+// [row0, row0 + TR), for the rows below n that are not skipped, into its swizzled place.
 template <typename Cfg>
 __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cache, RowSrc rows, int row0, int n,
                                            unsigned char* buf) {
@@ -62,94 +66,59 @@ __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cac
     if (row < n) {
       const uint32_t id = rows.get(row);
       if (id != 0xffffffffu)
-        cp_async16(buf + rr * Cfg::ROWB + ch * 16, cache + (size_t)id * Cfg::ROWB + ch * 16);
+        cp_async16(buf + rr * Cfg::ROWB + Cfg::swz(rr, ch) * 16, cache + (size_t)id * Cfg::ROWB + ch * 16);
     }
   }
 }
 
-// This lane's 8 dims of row `rr` of a staged tile (chunk li, and li + 16 for fp32) as 4 float pairs.
+// 16-byte chunk (logical index c) of staged row rr as 4 float pairs (bf16: 8 dims; fp32: 4 dims in pairs 0-1).
+template <typename KV_T, typename Cfg>
+__device__ __forceinline__ void chunk2(const unsigned char* buf, int rr, int c, float2* f) {
+  const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * Cfg::ROWB + Cfg::swz(rr, c) * 16);
+  if (sizeof(KV_T) == 2) {
+    f[0] = make_float2(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u));
+    f[1] = make_float2(__uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+    f[2] = make_float2(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u));
+    f[3] = make_float2(__uint_as_float(v.w << 16), __uint_as_float(v.w & 0xffff0000u));
+  } else {
+    f[0] = make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
+    f[1] = make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
+  }
+}
+
+// V sweep lane layout: lane li of a 16-lane row group owns chunk li (and li + 16 for fp32): 8 dims as 4 pairs.
 template <typename KV_T, typename Cfg>
 __device__ __forceinline__ void load_row2(const unsigned char* buf, int rr, int li, float2 (&f)[4]) {
 #pragma unroll
-  for (int c = 0; c < Cfg::NCL; ++c) {
-    const uint4 v = *reinterpret_cast<const uint4*>(buf + rr * Cfg::ROWB + (li + 16 * c) * 16);
-    if (sizeof(KV_T) == 2) {
-      f[0] = make_float2(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u));
-      f[1] = make_float2(__uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
-      f[2] = make_float2(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u));
-      f[3] = make_float2(__uint_as_float(v.w << 16), __uint_as_float(v.w & 0xffff0000u));
-    } else {
-      f[2 * c] = make_float2(__uint_as_float(v.x), __uint_as_float(v.y));
-      f[2 * c + 1] = make_float2(__uint_as_float(v.z), __uint_as_float(v.w));
-    }
-  }
+  for (int c = 0; c < Cfg::NCL; ++c) chunk2<KV_T, Cfg>(buf, rr, li + 16 * c, f + 2 * c);
 }
 
-// Dim held by lane li in slot e (0..7).
+// Dim held by lane li of a row group in slot e (0..7) in the V sweep.
 template <typename Cfg>
 __device__ __forceinline__ int lane_dim(int li, int e) {
   return (li + 16 * (e / Cfg::VE)) * Cfg::VE + (e % Cfg::VE);
 }
 
-// Head whose full 16-lane sum lane li holds after the transposed reduction (see reduce16).
-template <int HP>
-__device__ __forceinline__ int lane_head(int li) {
-  if (HP == 4) return ((li >> 3) & 1) * 2 + ((li >> 2) & 1);
-  if (HP == 2) return (li >> 3) & 1;
-  return 0;
-}
-
-// Sum HP partial values over the 16 lanes of a row group. Lane li ends with the total of head lane_head<HP>(li).
-template <int HP>
-__device__ __forceinline__ float reduce16(const float (&v)[HP], int li) {
-  if (HP == 4) {
-    const bool b3 = (li >> 3) & 1, b2 = (li >> 2) & 1;
-    float a0 = b3 ? v[2] : v[0], a1 = b3 ? v[3] : v[1];
-    const float s0 = b3 ? v[0] : v[2], s1 = b3 ? v[1] : v[3];
-    a0 += __shfl_xor_sync(0xffffffffu, s0, 8);
-    a1 += __shfl_xor_sync(0xffffffffu, s1, 8);
-    float b = b2 ? a1 : a0;
-    b += __shfl_xor_sync(0xffffffffu, b2 ? a0 : a1, 4);
-    b += __shfl_xor_sync(0xffffffffu, b, 2);
-    b += __shfl_xor_sync(0xffffffffu, b, 1);
-    return b;
-  } else if (HP == 2) {
-    const bool b3 = (li >> 3) & 1;
-    float a = b3 ? v[1] : v[0];
-    a += __shfl_xor_sync(0xffffffffu, b3 ? v[0] : v[1], 8);
-    a += __shfl_xor_sync(0xffffffffu, a, 4);
-    a += __shfl_xor_sync(0xffffffffu, a, 2);
-    a += __shfl_xor_sync(0xffffffffu, a, 1);
-    return a;
-  } else {
-    float a = v[0];
-    a += __shfl_xor_sync(0xffffffffu, a, 8);
-    a += __shfl_xor_sync(0xffffffffu, a, 4);
-    a += __shfl_xor_sync(0xffffffffu, a, 2);
-    a += __shfl_xor_sync(0xffffffffu, a, 1);
-    return a;
-  }
-}
-
-// Attend over rows[0, n_rows). q: this lane's 8 dims as 4 pairs, pre-multiplied by scale * log2(e). Writes the CTA
-// partial (s_m[HP], s_l[HP], s_acc[HP][128]) to shared memory; ends with a __syncthreads(). Dot products and the
-// p * v accumulation use Blackwell's paired fp32 FMA (two lanes of fp32 per instruction).
+// Attend over rows[0, n_rows). s_q: the heads' q (pre-multiplied by scale * log2 e), HP x 128 floats in shared
+// memory. Writes the CTA partial (s_m[HP], s_l[HP], s_acc[HP][128]); ends with a __syncthreads().
+// K sweep: thread (part, rr) = (tid / TR, tid % TR) accumulates the dot products of staged row rr over chunks
+// [part * KCH, (part + 1) * KCH) for every head (q reads are warp-uniform broadcasts); the KPARTS partial sums of a
+// row are added through shared memory. V sweep: 16 lanes per row, 8 dims per lane. Products use Blackwell's paired
+// fp32 FMA.
 template <typename KV_T, int HP>
 __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict__ Vf, RowSrc rows, int n_rows,
-                            const float2 (&q)[HP][4], unsigned char* dsm, int nstage, float* s_m, float* s_l,
-                            float* s_acc, unsigned* err) {
+                            const float* s_q, unsigned char* dsm, int nstage, float* s_m, float* s_l, float* s_acc) {
   using Cfg = AttendCfg<KV_T, HP>;
-  (void)err;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, li = lane & 15;
-  const int grp = tid >> 4;                              // row group 0..LG-1
+  const int grp = tid >> 4;                              // V sweep row group 0..LG-1
+  const int krow = tid % Cfg::TR, kpart = tid / Cfg::TR; // K sweep row and dim part
   unsigned char* stages = dsm;
   float* s_sc = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES);
-  float* s_wm = s_sc + Cfg::CHUNK * HP;                  // [kWarps][HP] warp maxima
+  float* s_kp = s_sc + Cfg::CHUNK * HP;                  // [KPARTS][TR][HP] partial dot products
+  float* s_wm = s_kp + Cfg::KPARTS * Cfg::TR * HP + HP * kHeadDim;   // [kWarps][HP] warp maxima
   float* s_wl = s_wm + kWarps * HP;                      // [kWarps][HP] warp sums of p
   const unsigned char* Kb = reinterpret_cast<const unsigned char*>(Kf);
   const unsigned char* Vb = reinterpret_cast<const unsigned char*>(Vf);
-  const int my_head = lane_head<HP>(li);
-  const bool head_writer = (li & (16 / HP - 1)) == 0;   // one lane per head in each row group
 
   float m_run[HP], l_run[HP];
   float2 acc[HP][4];
@@ -161,122 +130,166 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
     for (int i = 0; i < 4; ++i) acc[hh][i] = make_float2(0.f, 0.f);
   }
 
-  for (int c0 = 0; c0 < n_rows; c0 += Cfg::CHUNK) {
-    const int n = min(Cfg::CHUNK, n_rows - c0);
-    RowSrc rs = rows;
-    if (rs.list) rs.list += c0; else rs.base += (uint32_t)c0;
-    const int ntiles = (n + Cfg::TR - 1) / Cfg::TR;
-    float m_loc = -INFINITY;                            // max of this lane's head over its rows
-
-    // ---------------- K sweep ----------------
-    for (int s = 0; s < nstage - 1; ++s) {
-      if (s < ntiles) issue_tile<Cfg>(Kb, rs, s * Cfg::TR, n, stages + s * Cfg::STAGE_BYTES);
-      cp_async_commit();
+  // One continuous stream of tiles through the stage ring: for every chunk of up to CHUNK rows, its K tiles, then its
+  // V tiles. Loads run nstage - 1 tiles ahead across sweep and chunk boundaries, so the ring never drains.
+  struct Cursor {                                       // position in the tile stream
+    int c0, n, nt, v, t;                                // chunk start, chunk rows, chunk tiles, V sweep?, tile
+    __device__ __forceinline__ void start(int n_rows) { c0 = 0; n = min(Cfg::CHUNK, n_rows); nt = (n + Cfg::TR - 1) / Cfg::TR; v = 0; t = 0; }
+    __device__ __forceinline__ bool valid() const { return nt > 0; }
+    __device__ __forceinline__ void next(int n_rows) {
+      if (++t < nt) return;
+      t = 0;
+      if (!v) { v = 1; return; }
+      v = 0;
+      c0 += Cfg::CHUNK;
+      n = max(0, min(Cfg::CHUNK, n_rows - c0));
+      nt = (n + Cfg::TR - 1) / Cfg::TR;
     }
-    int scur = 0, snext = nstage - 1;                   // stage of tile t, stage the next issue fills
-    for (int t = 0; t < ntiles; ++t) {
-      cp_async_wait_dyn(nstage - 2);
-      __syncthreads();                                  // tile t landed for everyone; tile t-1's stage is free
-      const int tn = t + nstage - 1;
-      if (tn < ntiles) issue_tile<Cfg>(Kb, rs, tn * Cfg::TR, n, stages + snext * Cfg::STAGE_BYTES);
-      cp_async_commit();
-      const unsigned char* buf = stages + scur * Cfg::STAGE_BYTES;
-      scur = scur + 1 == nstage ? 0 : scur + 1;
-      snext = snext + 1 == nstage ? 0 : snext + 1;
+  };
+  auto chunk_rows = [&](const Cursor& cu) {
+    RowSrc r = rows;
+    if (r.list) r.list += cu.c0; else r.base += (uint32_t)cu.c0;
+    return r;
+  };
+  Cursor ci, cc;                                        // issue cursor, consume cursor
+  ci.start(n_rows);
+  cc.start(n_rows);
+  int sissue = 0, scons = 0;                            // stages of the next issue / consume
+  for (int s = 0; s < nstage - 1; ++s) {
+    if (ci.valid()) {
+      issue_tile<Cfg>(ci.v ? Vb : Kb, chunk_rows(ci), ci.t * Cfg::TR, ci.n, stages + sissue * Cfg::STAGE_BYTES);
+      ci.next(n_rows);
+    }
+    cp_async_commit();
+    sissue = sissue + 1 == nstage ? 0 : sissue + 1;
+  }
+  float m_loc = -INFINITY;                              // max of the (row, head) scores this thread reduced
+  while (cc.valid()) {
+    cp_async_wait_dyn(nstage - 2);
+    __syncthreads();                                    // this tile landed for everyone; the previous stage is free
+    if (ci.valid()) {
+      issue_tile<Cfg>(ci.v ? Vb : Kb, chunk_rows(ci), ci.t * Cfg::TR, ci.n, stages + sissue * Cfg::STAGE_BYTES);
+      ci.next(n_rows);
+    }
+    cp_async_commit();
+    sissue = sissue + 1 == nstage ? 0 : sissue + 1;
+    const unsigned char* buf = stages + scons * Cfg::STAGE_BYTES;
+    scons = scons + 1 == nstage ? 0 : scons + 1;
+    const RowSrc rs = chunk_rows(cc);
+    const int n = cc.n, t = cc.t;
+    if (!cc.v) {
+      // ---------------- K tile: partial dot products, then scores ----------------
+      {
+        const int row = t * Cfg::TR + krow;
+        const bool live = row < n && rs.get(row) != 0xffffffffu;
+        float2 a[HP];
 #pragma unroll
-      for (int i = 0; i < Cfg::RPG; ++i) {
-        const int rr = grp * Cfg::RPG + i;
-        const int row = t * Cfg::TR + rr;
-        const bool valid = row < n && rs.get(row) != 0xffffffffu;
-        float2 kf[4];
-        if (valid) load_row2<KV_T, Cfg>(buf, rr, li, kf);
-        else {
+        for (int hh = 0; hh < HP; ++hh) a[hh] = make_float2(0.f, 0.f);
+        if (live) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) kf[e] = make_float2(0.f, 0.f);
+          for (int j = 0; j < Cfg::KCH; ++j) {
+            const int c = kpart * Cfg::KCH + j;
+            float2 kf[4];
+            chunk2<KV_T, Cfg>(buf, krow, c, kf);
+#pragma unroll
+            for (int hh = 0; hh < HP; ++hh) {
+              const float4* qc = reinterpret_cast<const float4*>(s_q + hh * kHeadDim + c * Cfg::VE);
+              const float4 q0 = qc[0];
+              a[hh] = __ffma2_rn(make_float2(q0.x, q0.y), kf[0], a[hh]);
+              a[hh] = __ffma2_rn(make_float2(q0.z, q0.w), kf[1], a[hh]);
+              if (Cfg::VE == 8) {
+                const float4 q1 = qc[1];
+                a[hh] = __ffma2_rn(make_float2(q1.x, q1.y), kf[2], a[hh]);
+                a[hh] = __ffma2_rn(make_float2(q1.z, q1.w), kf[3], a[hh]);
+              }
+            }
+          }
         }
-        float part[HP];
+        float* kp = s_kp + (kpart * Cfg::TR + krow) * HP;
+        if (HP == 4) {
+          *reinterpret_cast<float4*>(kp) = make_float4(a[0].x + a[0].y, a[1 % HP].x + a[1 % HP].y,
+                                                       a[2 % HP].x + a[2 % HP].y, a[3 % HP].x + a[3 % HP].y);
+        } else {
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) kp[hh] = a[hh].x + a[hh].y;
+        }
+      }
+      __syncthreads();                                  // partial sums of the tile visible
+      for (int i = tid; i < Cfg::TR * HP; i += kThreads) {
+        const int rr = i / HP;
+        const int row = t * Cfg::TR + rr;
+        if (row < n) {
+          float sc = 0.f;
+#pragma unroll
+          for (int pp = 0; pp < Cfg::KPARTS; ++pp) sc += s_kp[pp * Cfg::TR * HP + i];
+          if (rs.get(row) == 0xffffffffu) sc = -INFINITY;
+          s_sc[row * HP + (i % HP)] = sc;
+          m_loc = fmaxf(m_loc, sc);
+        }
+      }
+      if (t == cc.nt - 1) {
+        // ---------------- end of the chunk's K tiles: chunk maximum, one rescale, p = exp2(s - m) ----------------
+        // thread tid reduced scores of head tid % HP
+        float mh[HP];
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) mh[hh] = (tid % HP == hh) ? m_loc : -INFINITY;
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh)
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) mh[hh] = fmaxf(mh[hh], __shfl_xor_sync(0xffffffffu, mh[hh], o));
+        if (lane == 0) {
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) s_wm[w * HP + hh] = mh[hh];
+        }
+        m_loc = -INFINITY;
+        __syncthreads();                                // scores + warp maxima visible
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh) {
-          float2 a = __fmul2_rn(q[hh][0], kf[0]);
-          a = __ffma2_rn(q[hh][1], kf[1], a);
-          a = __ffma2_rn(q[hh][2], kf[2], a);
-          a = __ffma2_rn(q[hh][3], kf[3], a);
-          part[hh] = a.x + a.y;
+          float mc = -INFINITY;
+#pragma unroll
+          for (int i = 0; i < kWarps; ++i) mc = fmaxf(mc, s_wm[i * HP + hh]);
+          const float mn = fmaxf(m_run[hh], mc);
+          const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run[hh] - mn);
+          m_run[hh] = mn;
+          l_run[hh] *= corr;
+          const float2 c2 = make_float2(corr, corr);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[hh][i] = __fmul2_rn(acc[hh][i], c2);
         }
-        float sc = reduce16<HP>(part, li);
-        if (!valid) sc = -INFINITY;
-        m_loc = fmaxf(m_loc, sc);
-        if (row < n && head_writer) s_sc[row * HP + my_head] = sc;
+        float psum[HP];
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) psum[hh] = 0.f;
+        for (int i = tid; i < n * HP; i += kThreads) {
+          const int hh = i % HP;
+          float mv = m_run[0];
+#pragma unroll
+          for (int x = 1; x < HP; ++x) mv = (hh == x) ? m_run[x] : mv;
+          const float sv = s_sc[i];
+          const float pv = (mv == -INFINITY || sv == -INFINITY) ? 0.f : exp2f(sv - mv);
+          s_sc[i] = pv;
+#pragma unroll
+          for (int x = 0; x < HP; ++x) psum[x] += (hh == x) ? pv : 0.f;
+        }
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) psum[hh] += __shfl_xor_sync(0xffffffffu, psum[hh], o);
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) s_wl[w * HP + hh] = psum[hh];
+        }
+        __syncthreads();                                // p and the sums visible
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) {
+          float sum = 0.f;
+#pragma unroll
+          for (int i = 0; i < kWarps; ++i) sum += s_wl[i * HP + hh];
+          l_run[hh] += sum;
+        }
       }
-    }
-    cp_async_wait<0>();
-
-    // ---------------- chunk maximum, one rescale, p = exp2(s - m) in place ----------------
-    m_loc = fmaxf(m_loc, __shfl_xor_sync(0xffffffffu, m_loc, 16));   // the other row group of the warp
-    if (lane < 16 && head_writer) s_wm[w * HP + my_head] = m_loc;
-    __syncthreads();                                    // scores + warp maxima visible; K tiles consumed
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) {
-      float mc = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < kWarps; ++i) mc = fmaxf(mc, s_wm[i * HP + hh]);
-      const float mn = fmaxf(m_run[hh], mc);
-      const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run[hh] - mn);
-      m_run[hh] = mn;
-      l_run[hh] *= corr;
-      const float2 c2 = make_float2(corr, corr);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[hh][i] = __fmul2_rn(acc[hh][i], c2);
-    }
-    // V prologue first, so the loads overlap the exp pass
-    for (int s = 0; s < nstage - 1; ++s) {
-      if (s < ntiles) issue_tile<Cfg>(Vb, rs, s * Cfg::TR, n, stages + s * Cfg::STAGE_BYTES);
-      cp_async_commit();
-    }
-    float psum[HP];
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) psum[hh] = 0.f;
-    for (int i = tid; i < n * HP; i += kThreads) {
-      const int hh = i % HP;
-      float mv = m_run[0];
-#pragma unroll
-      for (int x = 1; x < HP; ++x) mv = (hh == x) ? m_run[x] : mv;
-      const float sv = s_sc[i];
-      const float pv = (mv == -INFINITY || sv == -INFINITY) ? 0.f : exp2f(sv - mv);
-      s_sc[i] = pv;
-#pragma unroll
-      for (int x = 0; x < HP; ++x) psum[x] += (hh == x) ? pv : 0.f;
-    }
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) {
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) psum[hh] += __shfl_xor_sync(0xffffffffu, psum[hh], o);
-    }
-    if (lane == 0) {
-#pragma unroll
-      for (int hh = 0; hh < HP; ++hh) s_wl[w * HP + hh] = psum[hh];
-    }
-    __syncthreads();                                    // p and the sums visible
-#pragma unroll
-    for (int hh = 0; hh < HP; ++hh) {
-      float sum = 0.f;
-#pragma unroll
-      for (int i = 0; i < kWarps; ++i) sum += s_wl[i * HP + hh];
-      l_run[hh] += sum;
-    }
-
-    // ---------------- V sweep: acc += p * v ----------------
-    scur = 0;
-    snext = nstage - 1;
-    for (int t = 0; t < ntiles; ++t) {
-      cp_async_wait_dyn(nstage - 2);
-      __syncthreads();
-      const int tn = t + nstage - 1;
-      if (tn < ntiles) issue_tile<Cfg>(Vb, rs, tn * Cfg::TR, n, stages + snext * Cfg::STAGE_BYTES);
-      cp_async_commit();
-      const unsigned char* buf = stages + scur * Cfg::STAGE_BYTES;
-      scur = scur + 1 == nstage ? 0 : scur + 1;
-      snext = snext + 1 == nstage ? 0 : snext + 1;
+    } else {
+      // ---------------- V tile: acc += p * v ----------------
 #pragma unroll
       for (int i = 0; i < Cfg::RPG; ++i) {
         const int rr = grp * Cfg::RPG + i;
@@ -301,9 +314,10 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
         }
       }
     }
-    cp_async_wait<0>();
-    __syncthreads();   // V tiles and p consumed; the next chunk (or the reduction) may reuse the buffers
+    cc.next(n_rows);
   }
+  cp_async_wait<0>();
+  __syncthreads();   // every tile consumed; the reduction may reuse the stage buffers
 
   // ---------------- CTA reduction: 2 row groups per warp, then the warps ----------------
 #pragma unroll
@@ -377,20 +391,18 @@ __device__ void finish_output(KV_T* __restrict__ out, float* __restrict__ part, 
   if (CS > 1) cluster.sync();   // peers keep their shared memory alive until rank 0 has read it
 }
 
-// This lane's q dims (pre-scaled by scale*log2 e) for the heads of one (batch, group), as 4 pairs per head.
+// Write the heads' q, pre-scaled by scale*log2 e, into the engine's shared q buffer (HP x 128 floats; heads >= h
+// are zero). Must be followed by a __syncthreads() before attend_rows reads it.
 template <typename KV_T, int HP>
-__device__ __forceinline__ void load_q(const KV_T* __restrict__ qb, long long sh, int h, float scale_log2,
-                                       float2 (&q)[HP][4]) {
+__device__ __forceinline__ float* stage_q(unsigned char* dsm, int nstage, const KV_T* __restrict__ qb, long long sh,
+                                          int h, float scale_log2) {
   using Cfg = AttendCfg<KV_T, HP>;
-  const int li = threadIdx.x & 15;
-#pragma unroll
-  for (int hh = 0; hh < HP; ++hh)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float x = (hh < h) ? tof(qb[hh * sh + lane_dim<Cfg>(li, 2 * e)]) * scale_log2 : 0.f;
-      const float y = (hh < h) ? tof(qb[hh * sh + lane_dim<Cfg>(li, 2 * e + 1)]) * scale_log2 : 0.f;
-      q[hh][e] = make_float2(x, y);
-    }
+  float* s_q = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::CHUNK * HP + Cfg::KPARTS * Cfg::TR * HP;
+  for (int i = threadIdx.x; i < HP * kHeadDim; i += kThreads) {
+    const int hh = i / kHeadDim, d = i % kHeadDim;
+    s_q[i] = hh < h ? tof(qb[hh * sh + d]) * scale_log2 : 0.f;
+  }
+  return s_q;
 }
 
 }  // namespace al

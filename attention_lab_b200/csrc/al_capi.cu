@@ -141,7 +141,7 @@ size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 constexpr int kFusedStaticBytes = 40 * 1024;
 constexpr int kAttendStaticBytes = 4 * 1024;
 
-constexpr int kStages = 8;   // attend pipeline depth: registers already limit a 512-thread CTA to one per SM
+constexpr int kStages = 5;   // deepest attend pipeline (32 KB stages); registers limit a 512-thread CTA to one per SM
 
 int engine_smem(int kv_dtype, int hp, int stages = kStages) {
   switch (kv_dtype * 8 + hp) {
@@ -251,7 +251,7 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
     const size_t select_bytes = (size_t)p.keys_bytes + (size_t)p.ccap * 8;
     const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
     bool fits = false;
-    for (int st = kStages; st >= 4 && !fits; --st) {
+    for (int st = kStages; st >= 3 && !fits; --st) {
       const size_t eng = attend ? (size_t)engine_smem(kv_dtype, hp, st) : 0;
       p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
       smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;

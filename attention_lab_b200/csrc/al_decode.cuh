@@ -530,11 +530,12 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
 #undef CSYNC
 
   // ---------------- attend over this CTA's rows, then the cluster merge ----------------
-  float2 q[HP][4];
-  load_q<KV_T, HP>(reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg, p.q_sh, p.h, p.scale_log2, q);
+  const float* s_q = stage_q<KV_T, HP>(dsm, p.nstage, reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg,
+                                      p.q_sh, p.h, p.scale_log2);
+  __syncthreads();
   RowSrc rs{s_arow, 0u};
   attend_rows<KV_T, HP>(reinterpret_cast<const KV_T*>(p.k_cache), reinterpret_cast<const KV_T*>(p.v_cache), rs,
-                        fshare + n_sel, q, dsm, p.nstage, s_m, s_l, s_acc, p.err);
+                        fshare + n_sel, s_q, dsm, p.nstage, s_m, s_l, s_acc);
   finish_output<KV_T, HP>(p.out ? reinterpret_cast<KV_T*>(p.out) + (size_t)seg * p.h * kHeadDim : nullptr,
                           p.part ? p.part + (size_t)seg * p.h * (kHeadDim + 2) : nullptr, p.h, s_m, s_l, s_acc);
 }
@@ -578,10 +579,11 @@ __global__ void __launch_bounds__(kThreads, 1) attend_kernel(const AttendParams 
   } else {
     rs.base = (uint32_t)((long long)seg * p.C + r0);
   }
-  float2 q[HP][4];
-  load_q<KV_T, HP>(reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg, p.q_sh, p.h, p.scale_log2, q);
+  const float* s_q = stage_q<KV_T, HP>(dsm, p.nstage, reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg,
+                                      p.q_sh, p.h, p.scale_log2);
+  __syncthreads();
   attend_rows<KV_T, HP>(reinterpret_cast<const KV_T*>(p.k_cache), reinterpret_cast<const KV_T*>(p.v_cache), rs,
-                        r1 - r0, q, dsm, p.nstage, s_m, s_l, s_acc, p.err);
+                        r1 - r0, s_q, dsm, p.nstage, s_m, s_l, s_acc);
   finish_output<KV_T, HP>(p.out ? reinterpret_cast<KV_T*>(p.out) + (size_t)seg * p.h * kHeadDim : nullptr,
                           p.part ? p.part + (size_t)seg * p.h * (kHeadDim + 2) : nullptr, p.h, s_m, s_l, s_acc);
 }
