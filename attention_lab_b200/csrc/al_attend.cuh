@@ -107,7 +107,8 @@ __device__ __forceinline__ int lane_dim(int li, int e) {
 // fp32 FMA.
 template <typename KV_T, int HP>
 __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict__ Vf, RowSrc rows, int n_rows,
-                            const float* s_q, unsigned char* dsm, int nstage, float* s_m, float* s_l, float* s_acc) {
+                            const float* s_q, float scale_log2, unsigned char* dsm, int nstage, float* s_m, float* s_l,
+                            float* s_acc) {
   using Cfg = AttendCfg<KV_T, HP>;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5, li = lane & 15;
   const int grp = tid >> 4;                              // V sweep row group 0..LG-1
@@ -129,6 +130,22 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[hh][i] = make_float2(0.f, 0.f);
   }
+
+  // bf16 rows: q as the B operand of m16n8k16 (n = head, 8 heads with zeros beyond HP; k = 16 dims per step)
+  uint32_t qb[8][2];
+  if constexpr (sizeof(KV_T) == 2) {
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks) {
+      const float* qr = s_q + (g < HP ? g : 0) * kHeadDim + ks * 16 + 2 * t4;
+      const float z = g < HP ? 1.f : 0.f;
+      qb[ks][0] = pack_bf16x2(z * qr[0], z * qr[1]);
+      qb[ks][1] = pack_bf16x2(z * qr[8], z * qr[9]);
+    }
+  }
+  float mh[HP];                                         // per-head maxima of the scores this thread produced
+#pragma unroll
+  for (int hh = 0; hh < HP; ++hh) mh[hh] = -INFINITY;
 
   // One continuous stream of tiles through the stage ring: for every chunk of up to CHUNK rows, its K tiles, then its
   // V tiles. Loads run nstage - 1 tiles ahead across sweep and chunk boundaries, so the ring never drains.
@@ -163,7 +180,6 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
     cp_async_commit();
     sissue = sissue + 1 == nstage ? 0 : sissue + 1;
   }
-  float m_loc = -INFINITY;                              // max of the (row, head) scores this thread reduced
   while (cc.valid()) {
     cp_async_wait_dyn(nstage - 2);
     __syncthreads();                                    // this tile landed for everyone; the previous stage is free
@@ -178,61 +194,83 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
     const RowSrc rs = chunk_rows(cc);
     const int n = cc.n, t = cc.t;
     if (!cc.v) {
-      // ---------------- K tile: partial dot products, then scores ----------------
-      {
-        const int row = t * Cfg::TR + krow;
-        const bool live = row < n && rs.get(row) != 0xffffffffu;
-        float2 a[HP];
+      // ---------------- K tile: scores of its rows ----------------
+      if constexpr (sizeof(KV_T) == 2) {
+        // tensor cores: warp w < TR/16 owns rows [16w, 16w + 16) of the tile; 8 steps of 16 dims
+        if (w < Cfg::TR / 16) {
+          const int lr = 16 * w + (lane & 15), lhi = lane >> 4;
+          const uint32_t rowaddr = smem_addr(buf + lr * Cfg::ROWB);
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int hh = 0; hh < HP; ++hh) a[hh] = make_float2(0.f, 0.f);
-        if (live) {
+          for (int ks = 0; ks < 8; ++ks) {
+            uint32_t a0, a1, a2, a3;
+            ldmatrix_x4(rowaddr + (uint32_t)(Cfg::swz(lr, 2 * ks + lhi) << 4), a0, a1, a2, a3);
+            mma_bf16_16816(c, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+          }
+          // c0, c1: row 16w + g, heads 2 t4, 2 t4 + 1; c2, c3: row 16w + g + 8
+          const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-          for (int j = 0; j < Cfg::KCH; ++j) {
-            const int c = kpart * Cfg::KCH + j;
-            float2 kf[4];
-            chunk2<KV_T, Cfg>(buf, krow, c, kf);
+          for (int half = 0; half < 2; ++half) {
+            const int row = t * Cfg::TR + 16 * w + g + 8 * half;
+            if (row < n) {
+              const bool live = rs.get(row) != 0xffffffffu;
 #pragma unroll
-            for (int hh = 0; hh < HP; ++hh) {
-              const float4* qc = reinterpret_cast<const float4*>(s_q + hh * kHeadDim + c * Cfg::VE);
-              const float4 q0 = qc[0];
-              a[hh] = __ffma2_rn(make_float2(q0.x, q0.y), kf[0], a[hh]);
-              a[hh] = __ffma2_rn(make_float2(q0.z, q0.w), kf[1], a[hh]);
-              if (Cfg::VE == 8) {
-                const float4 q1 = qc[1];
-                a[hh] = __ffma2_rn(make_float2(q1.x, q1.y), kf[2], a[hh]);
-                a[hh] = __ffma2_rn(make_float2(q1.z, q1.w), kf[3], a[hh]);
+              for (int j = 0; j < 2; ++j) {
+                const int head = 2 * t4 + j;
+                if (head < HP) {
+                  const float sc = live ? c[2 * half + j] * scale_log2 : -INFINITY;
+                  s_sc[row * HP + head] = sc;
+#pragma unroll
+                  for (int hh = 0; hh < HP; ++hh) mh[hh] = (hh == head) ? fmaxf(mh[hh], sc) : mh[hh];
+                }
               }
             }
           }
         }
-        float* kp = s_kp + (kpart * Cfg::TR + krow) * HP;
-        if (HP == 4) {
-          *reinterpret_cast<float4*>(kp) = make_float4(a[0].x + a[0].y, a[1 % HP].x + a[1 % HP].y,
-                                                       a[2 % HP].x + a[2 % HP].y, a[3 % HP].x + a[3 % HP].y);
-        } else {
+      } else {
+        // CUDA cores (fp32 rows): thread (kpart, krow) sums its KCH chunks of row krow for every head; the KPARTS
+        // partial sums of a row are added through shared memory
+        {
+          const int row = t * Cfg::TR + krow;
+          const bool live = row < n && rs.get(row) != 0xffffffffu;
+          float2 a[HP];
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) a[hh] = make_float2(0.f, 0.f);
+          if (live) {
+#pragma unroll
+            for (int j = 0; j < Cfg::KCH; ++j) {
+              const int c = kpart * Cfg::KCH + j;
+              float2 kf[4];
+              chunk2<KV_T, Cfg>(buf, krow, c, kf);
+#pragma unroll
+              for (int hh = 0; hh < HP; ++hh) {
+                const float4 q0 = *reinterpret_cast<const float4*>(s_q + hh * kHeadDim + c * Cfg::VE);
+                a[hh] = __ffma2_rn(make_float2(q0.x, q0.y), kf[0], a[hh]);
+                a[hh] = __ffma2_rn(make_float2(q0.z, q0.w), kf[1], a[hh]);
+              }
+            }
+          }
+          float* kp = s_kp + (kpart * Cfg::TR + krow) * HP;
 #pragma unroll
           for (int hh = 0; hh < HP; ++hh) kp[hh] = a[hh].x + a[hh].y;
         }
-      }
-      __syncthreads();                                  // partial sums of the tile visible
-      for (int i = tid; i < Cfg::TR * HP; i += kThreads) {
-        const int rr = i / HP;
-        const int row = t * Cfg::TR + rr;
-        if (row < n) {
-          float sc = 0.f;
+        __syncthreads();                                // partial sums of the tile visible
+        for (int i = tid; i < Cfg::TR * HP; i += kThreads) {
+          const int rr = i / HP, head = i % HP;
+          const int row = t * Cfg::TR + rr;
+          if (row < n) {
+            float sc = 0.f;
 #pragma unroll
-          for (int pp = 0; pp < Cfg::KPARTS; ++pp) sc += s_kp[pp * Cfg::TR * HP + i];
-          if (rs.get(row) == 0xffffffffu) sc = -INFINITY;
-          s_sc[row * HP + (i % HP)] = sc;
-          m_loc = fmaxf(m_loc, sc);
+            for (int pp = 0; pp < Cfg::KPARTS; ++pp) sc += s_kp[pp * Cfg::TR * HP + i];
+            sc = rs.get(row) == 0xffffffffu ? -INFINITY : sc * scale_log2;
+            s_sc[row * HP + head] = sc;
+#pragma unroll
+            for (int hh = 0; hh < HP; ++hh) mh[hh] = (hh == head) ? fmaxf(mh[hh], sc) : mh[hh];
+          }
         }
       }
       if (t == cc.nt - 1) {
         // ---------------- end of the chunk's K tiles: chunk maximum, one rescale, p = exp2(s - m) ----------------
-        // thread tid reduced scores of head tid % HP
-        float mh[HP];
-#pragma unroll
-        for (int hh = 0; hh < HP; ++hh) mh[hh] = (tid % HP == hh) ? m_loc : -INFINITY;
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
@@ -241,7 +279,8 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 #pragma unroll
           for (int hh = 0; hh < HP; ++hh) s_wm[w * HP + hh] = mh[hh];
         }
-        m_loc = -INFINITY;
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) mh[hh] = -INFINITY;
         __syncthreads();                                // scores + warp maxima visible
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh) {
@@ -391,16 +430,16 @@ __device__ void finish_output(KV_T* __restrict__ out, float* __restrict__ part, 
   if (CS > 1) cluster.sync();   // peers keep their shared memory alive until rank 0 has read it
 }
 
-// Write the heads' q, pre-scaled by scale*log2 e, into the engine's shared q buffer (HP x 128 floats; heads >= h
-// are zero). Must be followed by a __syncthreads() before attend_rows reads it.
+// Write the heads' q into the engine's shared q buffer (HP x 128 floats; heads >= h are zero). Scores are scaled by
+// scale*log2 e after the dot products. Must be followed by a __syncthreads() before attend_rows reads it.
 template <typename KV_T, int HP>
 __device__ __forceinline__ float* stage_q(unsigned char* dsm, int nstage, const KV_T* __restrict__ qb, long long sh,
-                                          int h, float scale_log2) {
+                                          int h) {
   using Cfg = AttendCfg<KV_T, HP>;
   float* s_q = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::CHUNK * HP + Cfg::KPARTS * Cfg::TR * HP;
   for (int i = threadIdx.x; i < HP * kHeadDim; i += kThreads) {
     const int hh = i / kHeadDim, d = i % kHeadDim;
-    s_q[i] = hh < h ? tof(qb[hh * sh + d]) * scale_log2 : 0.f;
+    s_q[i] = hh < h ? tof(qb[hh * sh + d]) : 0.f;
   }
   return s_q;
 }

@@ -130,6 +130,25 @@ __device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity, unsign
     if (mbar_try_wait(bar, parity)) return;
 }
 
+// ------------------------------------------------------------------------------------------------ tensor cores
+// ldmatrix x4: four 8x8 bf16 matrices whose row addresses lanes 0-7, 8-15, 16-23, 24-31 supply.
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+// D += A (16x16 bf16, row) * B (16x8 bf16, col) with fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};\n"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 // ------------------------------------------------------------------------------------------------ block scans
 // Inclusive prefix sum of one int per thread over the whole CTA. `ws` holds kWarps ints of shared scratch.
 // Returns the inclusive sum; *total receives the CTA total. Contains two __syncthreads().

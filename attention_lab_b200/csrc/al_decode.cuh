@@ -531,11 +531,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
 
   // ---------------- attend over this CTA's rows, then the cluster merge ----------------
   const float* s_q = stage_q<KV_T, HP>(dsm, p.nstage, reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg,
-                                      p.q_sh, p.h, p.scale_log2);
+                                      p.q_sh, p.h);
   __syncthreads();
   RowSrc rs{s_arow, 0u};
   attend_rows<KV_T, HP>(reinterpret_cast<const KV_T*>(p.k_cache), reinterpret_cast<const KV_T*>(p.v_cache), rs,
-                        fshare + n_sel, s_q, dsm, p.nstage, s_m, s_l, s_acc);
+                        fshare + n_sel, s_q, p.scale_log2, dsm, p.nstage, s_m, s_l, s_acc);
   finish_output<KV_T, HP>(p.out ? reinterpret_cast<KV_T*>(p.out) + (size_t)seg * p.h * kHeadDim : nullptr,
                           p.part ? p.part + (size_t)seg * p.h * (kHeadDim + 2) : nullptr, p.h, s_m, s_l, s_acc);
 }
@@ -580,10 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1) attend_kernel(const AttendParams 
     rs.base = (uint32_t)((long long)seg * p.C + r0);
   }
   const float* s_q = stage_q<KV_T, HP>(dsm, p.nstage, reinterpret_cast<const KV_T*>(p.q) + b * p.q_sb + g * p.q_sg,
-                                      p.q_sh, p.h, p.scale_log2);
+                                      p.q_sh, p.h);
   __syncthreads();
   attend_rows<KV_T, HP>(reinterpret_cast<const KV_T*>(p.k_cache), reinterpret_cast<const KV_T*>(p.v_cache), rs,
-                        r1 - r0, s_q, dsm, p.nstage, s_m, s_l, s_acc);
+                        r1 - r0, s_q, p.scale_log2, dsm, p.nstage, s_m, s_l, s_acc);
   finish_output<KV_T, HP>(p.out ? reinterpret_cast<KV_T*>(p.out) + (size_t)seg * p.h * kHeadDim : nullptr,
                           p.part ? p.part + (size_t)seg * p.h * (kHeadDim + 2) : nullptr, p.h, s_m, s_l, s_acc);
 }
