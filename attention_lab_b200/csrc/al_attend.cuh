@@ -329,29 +329,35 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
       }
     } else {
       // ---------------- V tile: acc += p * v ----------------
+      // all of this row group's rows are read first (skipped rows contribute zeros), then accumulated
+      float2 vf[Cfg::RPG][4];
+      float pr[Cfg::RPG][HP];
 #pragma unroll
       for (int i = 0; i < Cfg::RPG; ++i) {
         const int rr = grp * Cfg::RPG + i;
         const int row = t * Cfg::TR + rr;
-        if (row < n && rs.get(row) != 0xffffffffu) {
-          float p[HP];
-          if (HP == 4) {
-            const float4 p4 = *reinterpret_cast<const float4*>(s_sc + row * HP);
-            p[0] = p4.x; p[1 % HP] = p4.y; p[2 % HP] = p4.z; p[3 % HP] = p4.w;
-          } else {
+        const bool ok = row < n && rs.get(row) != 0xffffffffu;
+        const int rrow = ok ? row : 0;
+        if (HP == 4) {
+          const float4 p4 = *reinterpret_cast<const float4*>(s_sc + rrow * HP);
+          pr[i][0] = ok ? p4.x : 0.f; pr[i][1 % HP] = ok ? p4.y : 0.f;
+          pr[i][2 % HP] = ok ? p4.z : 0.f; pr[i][3 % HP] = ok ? p4.w : 0.f;
+        } else {
 #pragma unroll
-            for (int hh = 0; hh < HP; ++hh) p[hh] = s_sc[row * HP + hh];
-          }
-          float2 vf[4];
-          load_row2<KV_T, Cfg>(buf, rr, li, vf);
-#pragma unroll
-          for (int hh = 0; hh < HP; ++hh) {
-            const float2 p2 = make_float2(p[hh], p[hh]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[hh][e] = __ffma2_rn(p2, vf[e], acc[hh][e]);
-          }
+          for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[rrow * HP + hh] : 0.f;
         }
+        load_row2<KV_T, Cfg>(buf, rr, li, vf[i]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vf[i][e] = ok ? vf[i][e] : make_float2(0.f, 0.f);
       }
+#pragma unroll
+      for (int i = 0; i < Cfg::RPG; ++i)
+#pragma unroll
+        for (int hh = 0; hh < HP; ++hh) {
+          const float2 p2 = make_float2(pr[i][hh], pr[i][hh]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[hh][e] = __ffma2_rn(p2, vf[i][e], acc[hh][e]);
+        }
     }
     cc.next(n_rows);
   }

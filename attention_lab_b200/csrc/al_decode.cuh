@@ -149,7 +149,7 @@ __device__ void scan_columns(const DecodeParams& p, int seg, int c0, int c1, int
   float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
   if (p.zvec) {
     constexpr int VW = V16<IDX_T>::n;
-    constexpr int RB = (VW == 8) ? 8 : 16;                  // rows in flight per thread (32-64 load registers)
+    constexpr int RB = 16;                                   // rows in flight per thread (64 load registers)
     const int a0 = (c0 / VW) * VW;
     const int ngr = (c1 - a0 + VW - 1) / VW;
     const float4* u4 = reinterpret_cast<const float4*>(s_u);
