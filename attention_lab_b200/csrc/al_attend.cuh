@@ -52,7 +52,7 @@ struct RowSrc {
 };
 
 // Every thread copies the same 16-byte chunk (tid % NCH) of rows tid / NCH + j * (kThreads / NCH) of the tile
-// [row0, row0 + TR), for the rows below n that are not skipped, into its swizzled place.
+// [row0, row0 + TR) into its swizzled place; rows at or beyond n, and skipped rows, are filled with zeros.
 template <typename Cfg>
 __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cache, RowSrc rows, int row0, int n,
                                            unsigned char* buf) {
@@ -63,11 +63,10 @@ __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cac
   for (int j = 0; j < CPT; ++j) {
     const int rr = r0 + j * RSTEP;
     const int row = row0 + rr;
-    if (row < n) {
-      const uint32_t id = rows.get(row);
-      if (id != 0xffffffffu)
-        cp_async16(buf + rr * Cfg::ROWB + Cfg::swz(rr, ch) * 16, cache + (size_t)id * Cfg::ROWB + ch * 16);
-    }
+    const uint32_t id = row < n ? rows.get(row) : 0xffffffffu;
+    unsigned char* dst = buf + rr * Cfg::ROWB + Cfg::swz(rr, ch) * 16;
+    if (id != 0xffffffffu) cp_async16(dst, cache + (size_t)id * Cfg::ROWB + ch * 16);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);   // rows not read hold zeros
   }
 }
 
@@ -122,7 +121,8 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
   const unsigned char* Vb = reinterpret_cast<const unsigned char*>(Vf);
 
   float m_run[HP], l_run[HP];
-  float2 acc[HP][4];
+  float2 acc[HP][4];                                    // fp32 rows: this lane's 8 dims per head
+  float oc[4] = {0.f, 0.f, 0.f, 0.f};                   // bf16 rows: O^T fragment (dims 16 (w & 7) + .., heads)
 #pragma unroll
   for (int hh = 0; hh < HP; ++hh) {
     m_run[hh] = -INFINITY;
@@ -294,6 +294,11 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           const float2 c2 = make_float2(corr, corr);
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[hh][i] = __fmul2_rn(acc[hh][i], c2);
+          if (sizeof(KV_T) == 2) {                      // O^T fragment columns are heads 2 t4 and 2 t4 + 1
+            const int t4 = lane & 3;
+            if (hh == 2 * t4) { oc[0] *= corr; oc[2] *= corr; }
+            if (hh == 2 * t4 + 1) { oc[1] *= corr; oc[3] *= corr; }
+          }
         }
         float psum[HP];
 #pragma unroll
@@ -328,66 +333,100 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
         }
       }
     } else {
-      // ---------------- V tile: acc += p * v ----------------
-      // all of this row group's rows are read first (skipped rows contribute zeros), then accumulated
-      float2 vf[Cfg::RPG][4];
-      float pr[Cfg::RPG][HP];
+      // ---------------- V tile: O += p * v ----------------
+      if constexpr (sizeof(KV_T) == 2) {
+        // tensor cores: O^T[dims x heads] += V^T[dims x rows] * P^T[rows x heads]. Warp w owns dims
+        // [16 (w & 7), +16) and the tile's rows [64 (w >> 3), +64) (4 steps of 16). Each p is split into a bf16 high
+        // part and a bf16 remainder (two MMAs), so p keeps about 16 mantissa bits; V is exact in bf16.
+        const int mb = w & 7, khalf = w >> 3;
+        const int g = lane >> 2, t4 = lane & 3;
+        const int vr_lane = (lane & 7) + ((lane >> 4) << 3), vc_lane = 2 * mb + ((lane >> 3) & 1);
 #pragma unroll
-      for (int i = 0; i < Cfg::RPG; ++i) {
-        const int rr = grp * Cfg::RPG + i;
-        const int row = t * Cfg::TR + rr;
-        const bool ok = row < n && rs.get(row) != 0xffffffffu;
-        const int rrow = ok ? row : 0;
-        if (HP == 4) {
-          const float4 p4 = *reinterpret_cast<const float4*>(s_sc + rrow * HP);
-          pr[i][0] = ok ? p4.x : 0.f; pr[i][1 % HP] = ok ? p4.y : 0.f;
-          pr[i][2 % HP] = ok ? p4.z : 0.f; pr[i][3 % HP] = ok ? p4.w : 0.f;
-        } else {
+        for (int kk = 0; kk < 4; ++kk) {
+          const int r16 = 64 * khalf + 16 * kk;           // first row of this step within the tile
+          const int vr = r16 + vr_lane;
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(smem_addr(buf + vr * Cfg::ROWB + Cfg::swz(vr, vc_lane) * 16), a0, a1, a2, a3);
+          float pv[4];
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const int row = t * Cfg::TR + r16 + 2 * t4 + (x & 1) + 8 * (x >> 1);
+            pv[x] = (g < HP && row < n) ? s_sc[row * HP + (g < HP ? g : 0)] : 0.f;
+          }
+          uint32_t bh0 = pack_bf16x2(pv[0], pv[1]), bh1 = pack_bf16x2(pv[2], pv[3]);
+          const __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(&bh0);
+          const __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(&bh1);
+          const uint32_t bl0 = pack_bf16x2(pv[0] - __low2float(h0), pv[1] - __high2float(h0));
+          const uint32_t bl1 = pack_bf16x2(pv[2] - __low2float(h1), pv[3] - __high2float(h1));
+          mma_bf16_16816(oc, a0, a1, a2, a3, bh0, bh1);
+          mma_bf16_16816(oc, a0, a1, a2, a3, bl0, bl1);
+        }
+      } else {
+        // CUDA cores (fp32 rows): 16 lanes per row, 8 dims per lane; the row group's rows are read first
+        float2 vf[Cfg::RPG][4];
+        float pr[Cfg::RPG][HP];
+#pragma unroll
+        for (int i = 0; i < Cfg::RPG; ++i) {
+          const int rr = grp * Cfg::RPG + i;
+          const int row = t * Cfg::TR + rr;
+          const bool ok = row < n && rs.get(row) != 0xffffffffu;
+          const int rrow = ok ? row : 0;
 #pragma unroll
           for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[rrow * HP + hh] : 0.f;
+          load_row2<KV_T, Cfg>(buf, rr, li, vf[i]);
         }
-        load_row2<KV_T, Cfg>(buf, rr, li, vf[i]);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) vf[i][e] = ok ? vf[i][e] : make_float2(0.f, 0.f);
+        for (int i = 0; i < Cfg::RPG; ++i)
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) {
+            const float2 p2 = make_float2(pr[i][hh], pr[i][hh]);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[hh][e] = __ffma2_rn(p2, vf[i][e], acc[hh][e]);
+          }
       }
-#pragma unroll
-      for (int i = 0; i < Cfg::RPG; ++i)
-#pragma unroll
-        for (int hh = 0; hh < HP; ++hh) {
-          const float2 p2 = make_float2(pr[i][hh], pr[i][hh]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[hh][e] = __ffma2_rn(p2, vf[i][e], acc[hh][e]);
-        }
     }
     cc.next(n_rows);
   }
   cp_async_wait<0>();
   __syncthreads();   // every tile consumed; the reduction may reuse the stage buffers
 
-  // ---------------- CTA reduction: 2 row groups per warp, then the warps ----------------
+  // ---------------- CTA reduction ----------------
+  float* red = reinterpret_cast<float*>(stages);
+  if constexpr (sizeof(KV_T) == 2) {
+    // bf16 rows: red[khalf][head][128] from the O^T fragments, then the two row halves are added
+    const int mb = w & 7, khalf = w >> 3, g = lane >> 2, t4 = lane & 3;
 #pragma unroll
-  for (int hh = 0; hh < HP; ++hh)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
-      acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
+    for (int x = 0; x < 4; ++x) {
+      const int head = 2 * t4 + (x & 1), dim = 16 * mb + g + 8 * (x >> 1);
+      if (head < HP) red[(khalf * HP + head) * kHeadDim + dim] = oc[x];
     }
-  float* red = reinterpret_cast<float*>(stages);           // [kWarps][HP][128]
-  if (lane < 16) {
+    __syncthreads();
+    for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) s_acc[idx] = red[idx] + red[HP * kHeadDim + idx];
+  } else {
+    // fp32 rows: 2 row groups per warp, then the warps
 #pragma unroll
     for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e)] = acc[hh][e].x;
-        red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e + 1)] = acc[hh][e].y;
+        acc[hh][e].x += __shfl_xor_sync(0xffffffffu, acc[hh][e].x, 16);
+        acc[hh][e].y += __shfl_xor_sync(0xffffffffu, acc[hh][e].y, 16);
       }
-  }
-  __syncthreads();
-  for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) {
-    float a = 0.f;
+    if (lane < 16) {
 #pragma unroll
-    for (int i = 0; i < kWarps; ++i) a += red[i * HP * kHeadDim + idx];
-    s_acc[idx] = a;
+      for (int hh = 0; hh < HP; ++hh)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e)] = acc[hh][e].x;
+          red[(w * HP + hh) * kHeadDim + lane_dim<Cfg>(li, 2 * e + 1)] = acc[hh][e].y;
+        }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) {
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < kWarps; ++i) a += red[i * HP * kHeadDim + idx];
+      s_acc[idx] = a;
+    }
   }
   if (tid < HP) {
     float mv = m_run[0], lv = l_run[0];
