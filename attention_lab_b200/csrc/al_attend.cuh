@@ -35,6 +35,7 @@ struct AttendCfg {
   static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4;
   static_assert(RED_BYTES <= MIN_STAGES * STAGE_BYTES, "warp reduction buffer aliases the stage buffers");
   static_assert(RPG >= 1 && TR % LG == 0 && KCH * KPARTS == NCH && KPARTS * TR == kThreads, "tile shape");
+  static_assert(CHUNK % TR == 0, "chunks hold whole tiles");
   // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | K partial sums |
   // q (pre-scaled) | warp maxima and sums
   static constexpr int TAIL = CHUNK * HP * 4 + KPARTS * TR * HP * 4 + HP * kHeadDim * 4 + 2 * kWarps * HP * 4;
@@ -59,13 +60,14 @@ __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cac
   constexpr int CPT = Cfg::TR * Cfg::NCH / kThreads;      // chunks per thread per tile
   constexpr int RSTEP = kThreads / Cfg::NCH;              // rows between a thread's chunks
   const int ch = threadIdx.x % Cfg::NCH, r0 = threadIdx.x / Cfg::NCH;
+  const unsigned char* src = cache + ch * 16;
 #pragma unroll
   for (int j = 0; j < CPT; ++j) {
     const int rr = r0 + j * RSTEP;
     const int row = row0 + rr;
     const uint32_t id = row < n ? rows.get(row) : 0xffffffffu;
     unsigned char* dst = buf + rr * Cfg::ROWB + Cfg::swz(rr, ch) * 16;
-    if (id != 0xffffffffu) cp_async16(dst, cache + (size_t)id * Cfg::ROWB + ch * 16);
+    if (id != 0xffffffffu) cp_async16(dst, src + (size_t)id * Cfg::ROWB);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);   // rows not read hold zeros
   }
 }
@@ -146,6 +148,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
   float mh[HP];                                         // per-head maxima of the scores this thread produced
 #pragma unroll
   for (int hh = 0; hh < HP; ++hh) mh[hh] = -INFINITY;
+  float mh2[2] = {-INFINITY, -INFINITY};                // bf16 rows: maxima of this lane's heads 2 t4, 2 t4 + 1
 
   // One continuous stream of tiles through the stage ring: for every chunk of up to CHUNK rows, its K tiles, then its
   // V tiles. Loads run nstage - 1 tiles ahead across sweep and chunk boundaries, so the ring never drains.
@@ -219,9 +222,8 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
                 const int head = 2 * t4 + j;
                 if (head < HP) {
                   const float sc = live ? c[2 * half + j] * scale_log2 : -INFINITY;
-                  s_sc[row * HP + head] = sc;
-#pragma unroll
-                  for (int hh = 0; hh < HP; ++hh) mh[hh] = (hh == head) ? fmaxf(mh[hh], sc) : mh[hh];
+                  s_sc[head * Cfg::CHUNK + row] = sc;
+                  mh2[j] = fmaxf(mh2[j], sc);
                 }
               }
             }
@@ -263,7 +265,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 #pragma unroll
             for (int pp = 0; pp < Cfg::KPARTS; ++pp) sc += s_kp[pp * Cfg::TR * HP + i];
             sc = rs.get(row) == 0xffffffffu ? -INFINITY : sc * scale_log2;
-            s_sc[row * HP + head] = sc;
+            s_sc[head * Cfg::CHUNK + row] = sc;
 #pragma unroll
             for (int hh = 0; hh < HP; ++hh) mh[hh] = (hh == head) ? fmaxf(mh[hh], sc) : mh[hh];
           }
@@ -271,6 +273,12 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
       }
       if (t == cc.nt - 1) {
         // ---------------- end of the chunk's K tiles: chunk maximum, one rescale, p = exp2(s - m) ----------------
+        if (sizeof(KV_T) == 2) {
+          const int t4 = lane & 3;
+#pragma unroll
+          for (int hh = 0; hh < HP; ++hh) mh[hh] = hh == 2 * t4 ? mh2[0] : (hh == 2 * t4 + 1 ? mh2[1] : mh[hh]);
+          mh2[0] = mh2[1] = -INFINITY;
+        }
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh)
 #pragma unroll
@@ -300,19 +308,29 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
             if (hh == 2 * t4 + 1) { oc[1] *= corr; oc[3] *= corr; }
           }
         }
+        // p for every (head, row) of the chunk's tiles (zero past the last row). bf16 rows: each pair of rows is
+        // rewritten in place as the packed B fragment {bf16 hi(p0), hi(p1), lo(p0), lo(p1)}, lo = p - hi.
         float psum[HP];
+        const int nr = cc.nt * Cfg::TR;                 // rows of the chunk's tiles
 #pragma unroll
-        for (int hh = 0; hh < HP; ++hh) psum[hh] = 0.f;
-        for (int i = tid; i < n * HP; i += kThreads) {
-          const int hh = i % HP;
-          float mv = m_run[0];
-#pragma unroll
-          for (int x = 1; x < HP; ++x) mv = (hh == x) ? m_run[x] : mv;
-          const float sv = s_sc[i];
-          const float pv = (mv == -INFINITY || sv == -INFINITY) ? 0.f : exp2f(sv - mv);
-          s_sc[i] = pv;
-#pragma unroll
-          for (int x = 0; x < HP; ++x) psum[x] += (hh == x) ? pv : 0.f;
+        for (int hh = 0; hh < HP; ++hh) {
+          psum[hh] = 0.f;
+          const float mv = m_run[hh];
+          float* sh = s_sc + hh * Cfg::CHUNK;
+          for (int rp = tid; rp < nr / 2; rp += kThreads) {
+            const float2 sv = *reinterpret_cast<const float2*>(sh + 2 * rp);
+            const float p0 = (2 * rp < n && mv != -INFINITY && sv.x != -INFINITY) ? exp2f(sv.x - mv) : 0.f;
+            const float p1 = (2 * rp + 1 < n && mv != -INFINITY && sv.y != -INFINITY) ? exp2f(sv.y - mv) : 0.f;
+            psum[hh] += p0 + p1;
+            if (sizeof(KV_T) == 2) {
+              const uint32_t hi = pack_bf16x2(p0, p1);
+              const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&hi);
+              const uint32_t lo = pack_bf16x2(p0 - __low2float(h2), p1 - __high2float(h2));
+              *reinterpret_cast<uint2*>(sh + 2 * rp) = make_uint2(hi, lo);
+            } else {
+              *reinterpret_cast<float2*>(sh + 2 * rp) = make_float2(p0, p1);
+            }
+          }
         }
 #pragma unroll
         for (int hh = 0; hh < HP; ++hh) {
@@ -347,19 +365,15 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           const int vr = r16 + vr_lane;
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4_trans(smem_addr(buf + vr * Cfg::ROWB + Cfg::swz(vr, vc_lane) * 16), a0, a1, a2, a3);
-          float pv[4];
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            const int row = t * Cfg::TR + r16 + 2 * t4 + (x & 1) + 8 * (x >> 1);
-            pv[x] = (g < HP && row < n) ? s_sc[row * HP + (g < HP ? g : 0)] : 0.f;
+          // B fragment of head g (zero beyond HP): rows r16 + 2 t4 (+1) and + 8 (+9), packed by the p pass
+          uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
+          if (g < HP) {
+            const float* ph = s_sc + g * Cfg::CHUNK + t * Cfg::TR + r16 + 2 * t4;
+            f0 = *reinterpret_cast<const uint2*>(ph);
+            f1 = *reinterpret_cast<const uint2*>(ph + 8);
           }
-          uint32_t bh0 = pack_bf16x2(pv[0], pv[1]), bh1 = pack_bf16x2(pv[2], pv[3]);
-          const __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(&bh0);
-          const __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(&bh1);
-          const uint32_t bl0 = pack_bf16x2(pv[0] - __low2float(h0), pv[1] - __high2float(h0));
-          const uint32_t bl1 = pack_bf16x2(pv[2] - __low2float(h1), pv[3] - __high2float(h1));
-          mma_bf16_16816(oc, a0, a1, a2, a3, bh0, bh1);
-          mma_bf16_16816(oc, a0, a1, a2, a3, bl0, bl1);
+          mma_bf16_16816(oc, a0, a1, a2, a3, f0.x, f1.x);
+          mma_bf16_16816(oc, a0, a1, a2, a3, f0.y, f1.y);
         }
       } else {
         // CUDA cores (fp32 rows): 16 lanes per row, 8 dims per lane; the row group's rows are read first
@@ -372,7 +386,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           const bool ok = row < n && rs.get(row) != 0xffffffffu;
           const int rrow = ok ? row : 0;
 #pragma unroll
-          for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[rrow * HP + hh] : 0.f;
+          for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[hh * Cfg::CHUNK + rrow] : 0.f;
           load_row2<KV_T, Cfg>(buf, rr, li, vf[i]);
         }
 #pragma unroll
