@@ -138,10 +138,13 @@ int pad_heads(int h) { return h <= 1 ? 1 : (h <= 2 ? 2 : 4); }
 size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Static shared memory of the fused kernel (upper bound used for the dynamic budget).
-constexpr int kFusedStaticBytes = 40 * 1024;
+constexpr int kFusedStaticBytes = 8 * 1024;
 constexpr int kAttendStaticBytes = 4 * 1024;
 
 constexpr int kStages = 5;   // deepest attend pipeline (32 KB stages); registers limit a 512-thread CTA to one per SM
+// The fused kernel keeps three stages: its selection code spills to local memory, and the L1 left beside a smaller
+// shared-memory carve-out holds those spills (measured: scan and selection faster, attend no slower than at five).
+constexpr int kFusedStages = 3;
 
 int engine_smem(int kv_dtype, int hp, int stages = kStages) {
   switch (kv_dtype * 8 + hp) {
@@ -238,21 +241,37 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
 
   const int hp = attend ? pad_heads(p.h) : 1;
   const int budget = di->max_smem_optin - kFusedStaticBytes;
-  // Shared memory per CTA: [keys | candidate list] aliased with the attend engine, then the attend row list.
-  // The cluster size is the automatic (or requested) one, grown while a CTA's share does not fit.
+  // Shared memory per CTA: the selection region [histogram | cluster slice | bitmaps | candidate list] aliased with
+  // the attend engine, then the attend row list. The candidate list takes whatever the engine leaves, and at least
+  // room for a typical filtered list (the first scan round, plus about ln(columns / round) * k later keys). The
+  // cluster size is the automatic (or requested) one, grown while a CTA's share does not fit.
   int cs = cluster > 0 ? cluster : auto_cluster(p.B * p.G, p.M, di->sms, 1 << 30);
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
+  const int round_cols = kThreads * (p.zvec ? 16 / ez : 1);
   size_t smem = 0;
   for (;; cs <<= 1) {
     p.cpc = (int)round_up((size_t)((p.M + cs - 1) / cs), 8);
     if (p.cpc == 0) p.cpc = 8;
-    p.keys_bytes = (p.scan || p.select_mode != 0) ? (int)round_up((size_t)(p.cpc + 24) * 4, 16) : 0;
-    p.ccap = p.select_mode == 1 ? std::min(p.cpc + 8, 2 * p.k + 1024) : 0;
-    const size_t select_bytes = (size_t)p.keys_bytes + (size_t)p.ccap * 8;
+    size_t sel_fixed = 0;
+    int cap_min = 0;
+    if (p.select_mode == 1) {
+      if (p.cpc > 65535) { if (cluster > 0 || cs >= kMaxCluster) return fail(AL_EUNSUPPORTED, "more than 65535 candidates per CTA (cluster %d)", cs); continue; }
+      p.nwp = (p.cpc + 30) / 32 + 1;
+      p.bm_off = 4096 * 4 + (cs > 1 ? (int)round_up((size_t)(4096 / cs) * 4, 16) : 0);
+      p.list_off = p.bm_off + (int)round_up((size_t)p.nwp * 8, 16);
+      sel_fixed = (size_t)p.list_off;
+      cap_min = std::min(p.cpc, round_cols + 6 * p.k + 1024);
+    }
     const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
     bool fits = false;
-    for (int st = kStages; st >= 3 && !fits; --st) {
+    for (int st = kFusedStages; st >= 3 && !fits; --st) {
       const size_t eng = attend ? (size_t)engine_smem(kv_dtype, hp, st) : 0;
+      p.cap = 0;
+      if (p.select_mode == 1) {
+        const size_t room = eng > sel_fixed ? (eng - sel_fixed) / 8 : 0;
+        p.cap = (int)std::min<size_t>((size_t)p.cpc, std::max<size_t>(room, (size_t)cap_min));
+      }
+      const size_t select_bytes = sel_fixed + (size_t)p.cap * 8;
       p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
       smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
       p.nstage = st;

@@ -9,11 +9,14 @@
 //   attention over exactly those rows              (decode.py:131-142)   gather-free, rows read in place
 //
 // A segment is served by a thread-block cluster of CS CTAs (CS in 1..16). CTA c owns a contiguous slice of the
-// candidate columns; its scores stay in its shared memory as order keys. The radix histograms are reduce-scattered
-// across the cluster through distributed shared memory, so the segment's exact k-th key is found without any global
-// scratch. Each CTA then attends over the candidates it selected plus a share of F, and the cluster merges the
-// partial softmax states (log-sum-exp) into the output. Nothing is written to global memory except the z column,
-// the output, and the optional row list and scores.
+// candidate columns. While it scans, each CTA counts its keys' top 12 bits and keeps only the keys that can still be
+// in the top-k: a running lower bound of the k-th key's bin, read from the partial histogram, filters the keys
+// appended to a short candidate list in shared memory (about k * (1 + ln(columns / round)) entries instead of one key
+// per column). The radix histograms are reduce-scattered across the cluster through distributed shared memory, so
+// the segment's exact k-th key is found without any global scratch; the chosen columns are marked in bitmaps and
+// emitted in position order. Each CTA then attends over the candidates it selected plus a share of F, and the cluster
+// merges the partial softmax states (log-sum-exp) into the output. Nothing is written to global memory except the
+// z column, the output, and the optional row list and scores.
 #pragma once
 #include "al_attend.cuh"
 
@@ -28,9 +31,10 @@ struct DecodeParams {
   int uvec;               // 1: r == 32 and 16-byte aligned wq_t (vector u prologue)
   int canonical;
   int cpc;                // candidate columns per CTA (a multiple of 8)
-  int union_bytes;        // bytes of the [keys | candidate list] / attend-engine union at the start of dynamic smem
-  int keys_bytes;         // bytes of the key array (the candidate list follows it)
-  int ccap;               // candidate-list capacity per CTA (entries)
+  int union_bytes;        // bytes of the selection / attend-engine union at the start of dynamic smem
+  int bm_off, list_off;   // selection region: bitmaps and candidate list offsets (histogram at 0, slice at 16 KB)
+  int nwp;                // words per selection bitmap
+  int cap;                // candidate-list capacity per CTA (entries)
   int nstage;             // attend pipeline depth (4..8)
   float scale_log2;
   long long total_rows;   // B*G*C rows in the flattened cache
@@ -137,98 +141,283 @@ __device__ void write_z_column(const DecodeParams& p, int b, int g) {
     reinterpret_cast<IDX_T*>(p.zT)[((size_t)seg * p.r + j) * p.C + p.write_col] = fromf<IDX_T>(acc);
 }
 
-// Scores of candidate columns [c0, c1) -> order keys. The key of column c is stored at s_keys[c - kbase] with
-// kbase = c0 rounded down to a multiple of 8, so every 16-byte group of keys is aligned; indices outside
-// [c0 - kbase, c1 - kbase) hold no valid key. When s_hist is given, also counts every valid key's top 12 bits into
-// it (the first radix digit, hidden under the scan's memory latency), and writes fp32 scores when requested. Vector path: each thread owns VW adjacent columns and streams all r rows of them with
-// 16-byte loads (8 or 16 rows in flight); u is read from shared memory as broadcast float4s.
+// Scores of candidate columns [c0, c1) -> order keys, handed to a sink. The scan runs in rounds of kThreads column
+// groups; every lane of every warp calls sink.put<VW>(col, keys, scores, mask) once per round (warp-convergent: the
+// sink may use warp collectives) with VW adjacent columns starting at `col` (bit e of `mask`: column col + e lies
+// in [c0, c1)), then sink.round_end(round). The scan is a call of its own so that its loads in flight get the
+// registers they need whatever the rest of the kernel holds (the caller saves its live values once). Recomputing a
+// column gives the same key bit for bit (same loads, same fused multiply-add order), so a sink may rescan. Vector
+// path: each thread owns VW adjacent columns and streams all r rows of them with 16-byte loads; u is read from
+// shared memory as broadcast float4s.
+struct ZSrc {                                              // a segment's index columns zT[b, g] ([r, C])
+  const void* z; int r, C, vec;                            // vec: 16-byte aligned rows
+};
+
+// Eight rows of a thread's VW columns: 16-byte loads, rows at or beyond r reread row r - 1 (u is zero there, and a
+// non-finite z in row r - 1 already makes the true score non-finite).
+template <typename IDX_T, bool FULLR>
+__device__ __forceinline__ void load_rows8(uint4 (&v)[8], const IDX_T* zc, int j0, int r, int C) {
+#pragma unroll
+  for (int jj = 0; jj < 8; ++jj) v[jj] = ldg_stream16(zc + (size_t)(FULLR ? j0 + jj : min(j0 + jj, r - 1)) * C);
+}
+
+// acc += u[j0 + x] * z[x] for the eight rows held in v (rows in ascending order: the same FMA order on every path).
 template <typename IDX_T>
-__device__ void scan_columns(const DecodeParams& p, int seg, int c0, int c1, int kbase, const float* s_u,
-                             uint32_t* s_keys, unsigned* s_hist) {
-  const IDX_T* zseg = reinterpret_cast<const IDX_T*>(p.zT) + (size_t)seg * p.r * p.C;
-  float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
-  if (p.zvec) {
-    constexpr int VW = V16<IDX_T>::n;
-    constexpr int RB = 16;                                   // rows in flight per thread (64 load registers)
-    const int a0 = (c0 / VW) * VW;
-    const int ngr = (c1 - a0 + VW - 1) / VW;
-    const float4* u4 = reinterpret_cast<const float4*>(s_u);
-#pragma unroll 1
-    for (int gi = threadIdx.x; gi < ngr; gi += kThreads) {
-      const int col = a0 + gi * VW;
-      const IDX_T* zc = zseg + col;
-      float2 acc2[VW / 2];
+__device__ __forceinline__ void fma_rows8(float2 (&acc2)[V16<IDX_T>::n / 2], const uint4 (&v)[8], const float* s_u,
+                                          int j0) {
+  constexpr int VW = V16<IDX_T>::n;
+  const float4* u4 = reinterpret_cast<const float4*>(s_u + j0);
 #pragma unroll
-      for (int e = 0; e < VW / 2; ++e) acc2[e] = make_float2(0.f, 0.f);
+  for (int jq = 0; jq < 8; jq += 4) {
+    const float4 uu = u4[jq / 4];
+    const float uj[4] = {uu.x, uu.y, uu.z, uu.w};
 #pragma unroll
-      for (int jb = 0; jb < kMaxR; jb += RB) {
-        uint4 v[RB];
+    for (int x = 0; x < 4; ++x) {
+      float f[VW];
+      unpack(v[jq + x], f, (const IDX_T*)nullptr);
+      const float2 u2 = make_float2(uj[x], uj[x]);
 #pragma unroll
-        for (int jj = 0; jj < RB; ++jj)
-          v[jj] = (jb + jj < p.r) ? ldg_stream16(zc + (size_t)(jb + jj) * p.C) : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-        for (int jq = 0; jq < RB; jq += 4) {
-          const float4 uu = u4[(jb + jq) / 4];
-          const float uj[4] = {uu.x, uu.y, uu.z, uu.w};
-#pragma unroll
-          for (int x = 0; x < 4; ++x) {
-            float f[VW];
-            unpack(v[jq + x], f, (const IDX_T*)nullptr);
-            const float2 u2 = make_float2(uj[x], uj[x]);
-#pragma unroll
-            for (int e = 0; e < VW / 2; ++e) acc2[e] = __ffma2_rn(u2, make_float2(f[2 * e], f[2 * e + 1]), acc2[e]);
-          }
-        }
-      }
-      float acc[VW];
-#pragma unroll
-      for (int e = 0; e < VW / 2; ++e) { acc[2 * e] = acc2[e].x; acc[2 * e + 1] = acc2[e].y; }
-      uint32_t kk[VW];
-#pragma unroll
-      for (int e = 0; e < VW; ++e) {
-        kk[e] = score_key(acc[e]);
-        const int c = col + e;
-        if (c >= c0 && c < c1) {
-          if (s_hist) atomicAdd(&s_hist[kk[e] >> 20], 1u);
-          if (so) so[c] = acc[e];
-        }
-      }
-#pragma unroll
-      for (int e = 0; e < VW; e += 4)
-        *reinterpret_cast<uint4*>(s_keys + (col - kbase) + e) = make_uint4(kk[e], kk[e + 1], kk[e + 2], kk[e + 3]);
-    }
-  } else {
-    for (int c = c0 + threadIdx.x; c < c1; c += kThreads) {
-      float a = 0.f;
-      for (int j = 0; j < p.r; ++j) a = fmaf(s_u[j], tof(zseg[(size_t)j * p.C + c]), a);
-      const uint32_t key = score_key(a);
-      s_keys[c - kbase] = key;
-      if (s_hist) atomicAdd(&s_hist[key >> 20], 1u);
-      if (so) so[c] = a;
+      for (int e = 0; e < VW / 2; ++e) acc2[e] = __ffma2_rn(u2, make_float2(f[2 * e], f[2 * e + 1]), acc2[e]);
     }
   }
 }
 
+template <typename IDX_T, bool FULLR, typename Sink>
+__device__ __noinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1, const float* s_u, Sink sink) {
+  const IDX_T* zseg = reinterpret_cast<const IDX_T*>(zs.z);
+  const int r = FULLR ? kMaxR : zs.r, C = zs.C;
+  if (zs.vec) {
+    // Software pipeline over 8-row batches (4 per round): two batches are always in flight, and each batch is
+    // multiplied while the next one loads; the next round's first two batches load during this round's last two.
+    // A thread past the end of the columns rereads column a0 and its results are masked.
+    constexpr int VW = V16<IDX_T>::n;
+    static_assert(kMaxR == 32, "four 8-row batches per round");
+    const int a0 = (c0 / VW) * VW;
+    const int ngr = (c1 - a0 + VW - 1) / VW;
+    const int nrounds = (ngr + kThreads - 1) / kThreads;
+    uint4 va[8], vb[8];
+    int gi = threadIdx.x;
+    const IDX_T* zc = zseg + (gi < ngr ? a0 + gi * VW : a0);
+    if (nrounds > 0) {
+      load_rows8<IDX_T, FULLR>(va, zc, 0, r, C);
+      load_rows8<IDX_T, FULLR>(vb, zc, 8, r, C);
+    }
+#pragma unroll 1
+    for (int round = 0; round < nrounds; ++round, gi += kThreads) {
+      const bool in = gi < ngr;
+      const int col = a0 + gi * VW;
+      const int gn = gi + kThreads;
+      const IDX_T* zn = zseg + (gn < ngr ? a0 + gn * VW : a0);
+      const bool more = round + 1 < nrounds;
+      float2 acc2[VW / 2];
+#pragma unroll
+      for (int e = 0; e < VW / 2; ++e) acc2[e] = make_float2(0.f, 0.f);
+      fma_rows8<IDX_T>(acc2, va, s_u, 0);
+      load_rows8<IDX_T, FULLR>(va, zc, 16, r, C);
+      fma_rows8<IDX_T>(acc2, vb, s_u, 8);
+      load_rows8<IDX_T, FULLR>(vb, zc, 24, r, C);
+      fma_rows8<IDX_T>(acc2, va, s_u, 16);
+      if (more) load_rows8<IDX_T, FULLR>(va, zn, 0, r, C);
+      fma_rows8<IDX_T>(acc2, vb, s_u, 24);
+      if (more) load_rows8<IDX_T, FULLR>(vb, zn, 8, r, C);
+      zc = zn;
+      float acc[VW];
+      uint32_t kk[VW];
+      unsigned vm = 0;
+#pragma unroll
+      for (int e = 0; e < VW / 2; ++e) { acc[2 * e] = acc2[e].x; acc[2 * e + 1] = acc2[e].y; }
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        kk[e] = score_key(acc[e]);
+        vm |= (in && col + e >= c0 && col + e < c1) ? (1u << e) : 0u;
+      }
+      sink.template put<VW>(col, kk, acc, vm);
+      sink.round_end(round);
+    }
+  } else {
+#pragma unroll 1
+    for (int cb = c0, round = 0; cb < c1; cb += kThreads, ++round) {
+      const int c = cb + threadIdx.x;
+      const bool in = c < c1;
+      float a = 0.f;
+      if (in)
+        for (int j = 0; j < r; ++j) a = fmaf(s_u[j], tof(zseg[(size_t)j * C + c]), a);
+      const uint32_t key = score_key(a);
+      sink.template put<1>(c, &key, &a, in ? 1u : 0u);
+      sink.round_end(round);
+    }
+  }
+}
+
+// r == 32 (every row real) takes a version without the row clamp.
+template <typename IDX_T, typename Sink>
+__device__ __forceinline__ void scan_columns(const ZSrc zs, int c0, int c1, const float* s_u, const Sink& sink) {
+  if (zs.r == kMaxR) scan_columns_impl<IDX_T, true>(zs, c0, c1, s_u, sink);
+  else scan_columns_impl<IDX_T, false>(zs, c0, c1, s_u, sink);
+}
+
+// Selection state of the fused kernel at fixed shared addresses (no registers needed to reach it): the dynamic
+// region starts with the 4096-bin histogram; the candidate count and the filter threshold are static.
+extern __shared__ __align__(128) unsigned char g_dsm[];
+__shared__ unsigned g_list_count, g_list_thr;
+
+__device__ __forceinline__ uint4 lds_volatile_u4(const void* p) {
+  uint4 r;
+  asm volatile("ld.volatile.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(smem_addr(p)));
+  return r;
+}
+
+// One warp raises the CTA's filter threshold *thr (a bin of the 12-bit key histogram) to the highest bin b whose
+// suffix count sum(hist[b..4095]) reaches k. The histogram is read while other warps still add to it: the counts
+// read are never above the final ones, so the result never exceeds the final bin of the k-th largest key (of the CTA,
+// and so of the whole cluster), and every key of a top-k bin passes the filter. The threshold only increases.
+__device__ void raise_threshold(const unsigned* hist, unsigned* thr, int k) {
+  const int lane = threadIdx.x & 31;
+  int t0 = 0;
+  if (lane == 0) t0 = (int)*reinterpret_cast<volatile unsigned*>(thr);
+  t0 = __shfl_sync(0xffffffffu, t0, 0);
+  unsigned cum = 0;
+  for (int top = 4095; top >= t0; top -= 128) {
+    const int lo = top - 4 * lane - 3;                       // this lane's bins lo..lo+3; lane 0 holds the highest
+    const uint4 v = lds_volatile_u4(hist + lo);
+    const unsigned ls = v.x + v.y + v.z + v.w;
+    const unsigned blk = __reduce_add_sync(0xffffffffu, ls);
+    if (cum + blk >= (unsigned)k) {
+      unsigned incl = ls;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const int L = __ffs(__ballot_sync(0xffffffffu, cum + incl >= (unsigned)k)) - 1;
+      int b = lo;
+      unsigned c = cum + incl - ls;
+      if ((c += v.w) >= (unsigned)k) b = lo + 3;
+      else if ((c += v.z) >= (unsigned)k) b = lo + 2;
+      else if ((c += v.y) >= (unsigned)k) b = lo + 1;
+      b = __shfl_sync(0xffffffffu, b, L);
+      if (lane == 0 && b > t0) *reinterpret_cast<volatile unsigned*>(thr) = (unsigned)b;
+      return;
+    }
+    cum += blk;
+  }
+}
+
+// First pass of the radix select: every valid key's top 12 bits are counted, and the keys whose bin is at or above
+// the running threshold are appended to the CTA's candidate list (keys[cap] then columns - kb [cap]; warp-aggregated:
+// one shared atomic per warp and round). The list keeps counting past its capacity so that an overflow is visible.
+template <bool SCORES>
+struct SinkFirst {
+  float* so; int list_off, cap, k, kb;
+  template <int VW>
+  __device__ __forceinline__ void put(int col, const uint32_t* kk, const float* sc, unsigned vm) {
+    unsigned* hist = reinterpret_cast<unsigned*>(g_dsm);
+    const unsigned t = *reinterpret_cast<volatile unsigned*>(&g_list_thr);
+    unsigned pm = 0;
+#pragma unroll
+    for (int e = 0; e < VW; ++e)
+      if ((vm >> e) & 1u) {
+        atomicAdd(&hist[kk[e] >> 20], 1u);
+        if (SCORES) so[col + e] = sc[e];
+        if ((kk[e] >> 20) >= t) pm |= 1u << e;
+      }
+    if (__any_sync(0xffffffffu, pm != 0u)) {
+      // slots ordered by (e, lane): the lanes' stores of one e are contiguous (no bank conflicts)
+      const unsigned lt = (1u << (threadIdx.x & 31)) - 1u;
+      unsigned bal[VW];
+      unsigned tot = 0;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        bal[e] = __ballot_sync(0xffffffffu, (pm >> e) & 1u);
+        tot += __popc(bal[e]);
+      }
+      unsigned base = 0;
+      if ((threadIdx.x & 31) == 0) base = atomicAdd(&g_list_count, tot);
+      base = __shfl_sync(0xffffffffu, base, 0);
+      uint32_t* lkey = reinterpret_cast<uint32_t*>(g_dsm + list_off);
+      uint32_t* lcol = lkey + cap;
+#pragma unroll
+      for (int e = 0; e < VW; ++e) {
+        const unsigned o = base + __popc(bal[e] & lt);
+        if (((pm >> e) & 1u) && o < (unsigned)cap) {
+          lkey[o] = kk[e];
+          lcol[o] = (uint32_t)(col + e - kb);
+        }
+        base += __popc(bal[e]);
+      }
+    }
+  }
+  // every warp tightens the threshold after the first round (its keys were all appended), then one warp per round
+  __device__ __forceinline__ void round_end(int round) {
+    if (round == 0 || (int)(threadIdx.x >> 5) == round % kWarps)
+      raise_threshold(reinterpret_cast<const unsigned*>(g_dsm), &g_list_thr, k);
+  }
+};
+
+// Rescan sink, used when some CTA's candidate list overflowed: either a 10-bit digit histogram of the keys under a
+// prefix (marks == false), or the selection marks (bitmaps over columns - kb of the keys above and equal to tau).
+struct SinkRescan {
+  bool marks;
+  unsigned* hist; uint32_t prefix, pmask; int shift;
+  uint32_t* gt; uint32_t* eq; uint32_t tau; int kb;
+  template <int VW>
+  __device__ __forceinline__ void put(int col, const uint32_t* kk, const float*, unsigned vm) {
+    if (!marks) {
+#pragma unroll
+      for (int e = 0; e < VW; ++e)
+        if (((vm >> e) & 1u) && (kk[e] & pmask) == prefix) atomicAdd(&hist[(kk[e] >> shift) & 1023u], 1u);
+      return;
+    }
+    unsigned gm = 0, em = 0;
+#pragma unroll
+    for (int e = 0; e < VW; ++e)
+      if ((vm >> e) & 1u) {
+        gm |= (kk[e] > tau) ? (1u << e) : 0u;
+        em |= (kk[e] == tau) ? (1u << e) : 0u;
+      }
+    const int rel = col - kb;                                // a multiple of VW: the VW bits share one word
+    if (gm) atomicOr(&gt[rel >> 5], gm << (rel & 31));
+    if (em) atomicOr(&eq[rel >> 5], em << (rel & 31));
+  }
+  __device__ __forceinline__ void round_end(int) {}
+};
+
+// Scores only (no top-k): write the fp32 scores.
+struct SinkScores {
+  float* so;
+  template <int VW>
+  __device__ __forceinline__ void put(int col, const uint32_t*, const float* sc, unsigned vm) {
+#pragma unroll
+    for (int e = 0; e < VW; ++e)
+      if ((vm >> e) & 1u) so[col + e] = sc[e];
+  }
+  __device__ __forceinline__ void round_end(int) {}
+};
+
 // Cluster-wide pivot search over the CTAs' NB-bin histograms (complete and visible cluster-wide on entry): the bin
 // holding the need-th largest element counted from the top bin, and the number of elements in the bins above it.
-// Every CTA returns the same result. CS == 1 uses block barriers only.
+// Every CTA returns the same result. CS == 1 reads its own histogram and uses block barriers only; CS > 1 sums this
+// CTA's slice of the bins over the cluster into s_slice first.
 __device__ void pivot_round(cg::cluster_group& cluster, int CS, int crank, const unsigned* s_hist, unsigned* s_slice,
                             int* s_sltot, int* s_piv, int* s_ws, int NB, int need, int& bin_out, int& above_out) {
   const int tid = threadIdx.x;
   const int SL = NB / CS, s0 = crank * SL;
-  for (int i = tid; i < SL; i += kThreads) {
-    unsigned v = 0;
-    if (CS == 1) v = s_hist[i];
-    else
+  const unsigned* sl = s_hist;
+  if (CS > 1) {
+    for (int i = tid; i < SL; i += kThreads) {
+      unsigned v = 0;
       for (int c = 0; c < CS; ++c) v += cluster.map_shared_rank(s_hist, c)[s0 + i];
-    s_slice[i] = v;
+      s_slice[i] = v;
+    }
+    __syncthreads();
+    sl = s_slice;
   }
-  __syncthreads();
   const int BPT = (SL + kThreads - 1) / kThreads;
   int lsum = 0;
   for (int i = 0; i < BPT; ++i) {
     const int bin = tid * BPT + i;
-    if (bin < SL) lsum += (int)s_slice[bin];
+    if (bin < SL) lsum += (int)sl[bin];
   }
   int tot;
   const int incl = block_inclusive_scan(lsum, s_ws, &tot);
@@ -249,7 +438,7 @@ __device__ void pivot_round(cg::cluster_group& cluster, int CS, int crank, const
     for (int i = BPT - 1; i >= 0; --i) {
       const int bin = tid * BPT + i;
       if (bin < SL) {
-        const int hv = (int)s_slice[bin];
+        const int hv = (int)sl[bin];
         if (above < nd && above + hv >= nd) {
           if (CS == 1) { s_piv[0] = s0 + bin; s_piv[1] = cum + above; }
           else
@@ -270,11 +459,9 @@ __device__ void pivot_round(cg::cluster_group& cluster, int CS, int crank, const
 
 template <typename KV_T, typename IDX_T, int HP>
 __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodeParams p) {
-  extern __shared__ __align__(128) unsigned char dsm[];
+  unsigned char* dsm = g_dsm;
   __shared__ __align__(16) float s_u[kMaxR];
   __shared__ float s_pre[kWarps * 32];
-  __shared__ unsigned s_hist[4096];
-  __shared__ unsigned s_slice[4096];
   __shared__ int s_sltot[kMaxCluster];
   __shared__ int s_cgt[kMaxCluster], s_ceq[kMaxCluster], s_cflag[kMaxCluster];
   __shared__ int s_piv[2];
@@ -289,121 +476,108 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
   const int seg = blockIdx.y;
   const int b = seg / p.G, g = seg - b * p.G;
   const int tid = threadIdx.x;
-  // dynamic shared memory: [keys | candidate list] aliasing [attend engine], then the attend row list
-  uint32_t* s_keys = reinterpret_cast<uint32_t*>(dsm);
-  uint32_t* cand_key = reinterpret_cast<uint32_t*>(dsm + p.keys_bytes);
-  uint32_t* cand_idx = cand_key + p.ccap;
+  // dynamic shared memory: [histogram | cluster slice | selection bitmaps | candidate list] aliasing [attend engine],
+  // then the attend row list
+  unsigned* s_hist = reinterpret_cast<unsigned*>(dsm);
+  unsigned* s_slice = reinterpret_cast<unsigned*>(dsm + 4096 * 4);
+  uint32_t* s_gt = reinterpret_cast<uint32_t*>(dsm + p.bm_off);
+  uint32_t* s_eq = s_gt + p.nwp;
+  const uint32_t* s_lkey = reinterpret_cast<const uint32_t*>(dsm + p.list_off);
+  const uint32_t* s_lcol = s_lkey + p.cap;
   uint32_t* s_arow = reinterpret_cast<uint32_t*>(dsm + p.union_bytes);
 #define CSYNC() do { if (CS > 1) cluster.sync(); else __syncthreads(); } while (0)
-
-  // ---------------- prologue: z column (rank 0 of the cluster) and u ----------------
-  if (p.select_mode == 1)
-    for (int i = tid; i < 4096; i += kThreads) s_hist[i] = 0u;
-  if (p.k_new && crank == 0) write_z_column<IDX_T>(p, b, g);
-  if (p.scan) compute_u<IDX_T>(p, b, g, s_u, s_pre);
 
   const int c0 = p.lo + crank * p.cpc;
   const int c1 = min(p.hi, c0 + p.cpc);
   const int nloc = max(0, c1 - c0);
-  const int kbase = (c0 / 8) * 8, koff = c0 - kbase;
+  const int kb = (c0 / 32) * 32;                        // bitmap bit i and list column i stand for column kb + i
 
-  // ---------------- scan: candidate scores -> order keys, plus the histogram of their top 12 bits ----------------
-  if (p.scan && nloc > 0)
-    scan_columns<IDX_T>(p, seg, c0, c1, kbase, s_u, s_keys, p.select_mode == 1 ? s_hist : nullptr);
+  // ---------------- prologue: z column (rank 0 of the cluster) and u ----------------
+  if (p.select_mode == 1) {
+    for (int i = tid; i < 4096; i += kThreads) s_hist[i] = 0u;
+    for (int i = tid; i < 2 * p.nwp; i += kThreads) s_gt[i] = 0u;   // s_eq follows s_gt
+    if (tid == 0) { g_list_count = 0u; g_list_thr = 0u; }
+  }
+  if (p.k_new && crank == 0) write_z_column<IDX_T>(p, b, g);
+  if (p.scan) compute_u<IDX_T>(p, b, g, s_u, s_pre);     // ends with __syncthreads()
+
+  // ---------------- scan: candidate scores -> order keys ----------------
+  float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
+  const ZSrc zsrc{reinterpret_cast<const IDX_T*>(p.zT) + (size_t)seg * p.r * p.C, p.r, p.C, p.zvec};
+  if (p.scan && nloc > 0) {
+    if (p.select_mode == 1) {
+      if (so) {
+        SinkFirst<true> sk{so, p.list_off, p.cap, p.k, kb};
+        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+      } else {
+        SinkFirst<false> sk{nullptr, p.list_off, p.cap, p.k, kb};
+        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+      }
+    } else {
+      SinkScores sk{so};
+      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+    }
+  }
   CSYNC();
 
-  // key quads [q0, q1) cover the valid key indices [koff, koff + nloc); thread runs use an odd stride so the 8
-  // threads of a quarter warp read 8 different bank groups
-  const int q0 = koff / 4, q1 = (koff + nloc + 3) / 4;
-  const int QPT = (((q1 - q0) + kThreads - 1) / kThreads) | 1;
-  const int tq0 = min(q1, q0 + tid * QPT), tq1 = min(q1, tq0 + QPT);
-  const uint4* keys4 = reinterpret_cast<const uint4*>(s_keys);
-
   // ---------------- radix select of the k-th largest key over the cluster ----------------
-  // 1) the histogram of the top 12 key bits (built during the scan) gives the pivot bin b0;
-  // 2) one ordered pass copies every key with top bits >= b0 into a short candidate list (k plus the pivot bin);
-  // 3) two 10-bit passes over the list's pivot-bin keys find the exact k-th key tau and how many of its copies
-  //    (k_rem, in position order) complete the top-k. If some CTA's list would overflow, steps 2-3 run over the
-  //    full key array instead.
+  // 1) the histogram of the top 12 key bits gives the pivot bin b0; the candidate list holds every key of bin >= b0
+  //    (the scan's threshold never passed b0);
+  // 2) two 10-bit passes over the list's keys of bin b0 find the exact k-th key tau and how many of its copies
+  //    (k_rem, in position order) complete the top-k;
+  // 3) the chosen columns are marked in two bitmaps (key > tau, key == tau).
+  // If some CTA's list overflowed (heavy ties), steps 2-3 rescan the index columns instead of reading the list.
   uint32_t tau = 0;
   int k_rem = 0;
-  bool use_list = false;
-  int n_cand = 0;
   if (p.select_mode == 1) {
     int b0, gt0;
     pivot_round(cluster, CS, crank, s_hist, s_slice, s_sltot, s_piv, s_ws, 4096, p.k, b0, gt0);
-    const int need0 = p.k - gt0;
-    // candidate count of this thread's run, then its offset in the CTA's list
-    int cnt = 0;
-    for (int qi = tq0; qi < tq1; ++qi) {
-      const uint4 k4 = keys4[qi];
-      const uint32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int idx = qi * 4 + e;
-        cnt += (idx >= koff && idx < koff + nloc && (int)(kv[e] >> 20) >= b0) ? 1 : 0;
-      }
-    }
-    int ctot;
-    const int cinc = block_inclusive_scan(cnt, s_ws, &ctot);
+    const unsigned cnt = g_list_count;
+    bool use_list;
     if (CS > 1) {
-      if (tid < CS) cluster.map_shared_rank(s_cflag, tid)[crank] = ctot > p.ccap ? 1 : 0;
+      if (tid < CS) cluster.map_shared_rank(s_cflag, tid)[crank] = cnt > (unsigned)p.cap ? 1 : 0;
       cluster.sync();
       use_list = true;
       for (int c = 0; c < CS; ++c) use_list = use_list && s_cflag[c] == 0;
     } else {
-      use_list = ctot <= p.ccap;
+      use_list = cnt <= (unsigned)p.cap;
     }
-    if (use_list) {
-      int o = cinc - cnt;
-      for (int qi = tq0; qi < tq1; ++qi) {
-        const uint4 k4 = keys4[qi];
-        const uint32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int idx = qi * 4 + e;
-          if (idx >= koff && idx < koff + nloc && (int)(kv[e] >> 20) >= b0) {
-            cand_key[o] = kv[e];
-            cand_idx[o] = (uint32_t)idx;
-            ++o;
-          }
-        }
-      }
-      n_cand = ctot;
-    }
-    // refinement over the keys of bin b0: bits 19..10, then 9..0
+    const int n_list = use_list ? (int)cnt : 0;
     uint32_t prefix = (uint32_t)b0 << 20, pmask = 0xfff00000u;
-    k_rem = need0;
+    k_rem = p.k - gt0;
+    // passes 0 and 1: digits 19..10 and 9..0 of the keys under the prefix; pass 2: the marks
 #pragma unroll 1
-    for (int pass = 0; pass < 2; ++pass) {
+    for (int pass = 0; pass < 3; ++pass) {
       const int shift = pass == 0 ? 10 : 0;
-      for (int i = tid; i < 1024; i += kThreads) s_hist[i] = 0u;
-      __syncthreads();
+      if (pass < 2) {
+        for (int i = tid; i < 1024; i += kThreads) s_hist[i] = 0u;
+        __syncthreads();
+      }
       if (use_list) {
-        for (int i = tid; i < n_cand; i += kThreads) {
-          const uint32_t key = cand_key[i];
-          if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & 1023u], 1u);
-        }
-      } else {
-        for (int qi = tq0; qi < tq1; ++qi) {
-          const uint4 k4 = keys4[qi];
-          const uint32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int idx = qi * 4 + e;
-            if (idx >= koff && idx < koff + nloc && (kv[e] & pmask) == prefix)
-              atomicAdd(&s_hist[(kv[e] >> shift) & 1023u], 1u);
+        for (int i = tid; i < n_list; i += kThreads) {
+          const uint32_t key = s_lkey[i];
+          if (pass < 2) {
+            if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & 1023u], 1u);
+          } else if (key >= prefix) {
+            const uint32_t c = s_lcol[i];
+            atomicOr(key > prefix ? &s_gt[c >> 5] : &s_eq[c >> 5], 1u << (c & 31));
           }
         }
+      } else if (nloc > 0) {
+        SinkRescan sk{pass == 2, s_hist, prefix, pmask, shift, s_gt, s_eq, prefix, kb};
+        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
       }
-      CSYNC();
-      int bn, above;
-      pivot_round(cluster, CS, crank, s_hist, s_slice, s_sltot, s_piv, s_ws, 1024, k_rem, bn, above);
-      prefix |= (uint32_t)bn << shift;
-      pmask |= 1023u << shift;
-      k_rem -= above;
+      if (pass < 2) {
+        CSYNC();
+        int bn, above;
+        pivot_round(cluster, CS, crank, s_hist, s_slice, s_sltot, s_piv, s_ws, 1024, k_rem, bn, above);
+        prefix |= (uint32_t)bn << shift;
+        pmask |= 1023u << shift;
+        k_rem -= above;
+      }
     }
     tau = prefix;
+    __syncthreads();
   }
 
   // ---------------- ordered selection: chosen candidates in ascending position order ----------------
@@ -416,32 +590,27 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
       for (int i = 0; i < F; ++i) fp += (p.fixed_rows[(size_t)seg * F + i] < seg_off) ? 1 : 0;
     s_fpre = fp;
   }
+  __syncthreads();
+  const int out_base = p.canonical ? s_fpre : F;
+  long long* ro = p.rows_out ? p.rows_out + (size_t)seg * p.S + out_base : nullptr;
   int n_sel = 0;
-  if (p.select_mode != 0) {
-    const bool all = p.select_mode == 2;
-    // this thread's entries: a run of the candidate list, or its run of key quads
-    const int EPT = ((n_cand + kThreads - 1) / kThreads) | 1;
-    const int te0 = min(n_cand, tid * EPT), te1 = min(n_cand, te0 + EPT);
+  if (p.select_mode == 2) {
+    // every candidate: column c has rank c - lo
+    n_sel = nloc;
+    for (int c = c0 + tid; c < c1; c += kThreads) {
+      const long long row = seg_off + (long long)(c - p.lo);
+      if (ro) ro[c - p.lo] = row;
+      s_arow[fshare + (c - c0)] = checked_row(row, p.total_rows, p.err);
+    }
+  } else if (p.select_mode == 1) {
+    // this thread's run of bitmap words (odd run length: the 8 threads of a quarter warp hit different banks)
+    const int nw = nloc > 0 ? (c1 - kb + 31) >> 5 : 0;
+    const int EPT = ((nw + kThreads - 1) / kThreads) | 1;
+    const int tw0 = min(nw, tid * EPT), tw1 = min(nw, tw0 + EPT);
     int cgt = 0, ceq = 0;
-    if (use_list) {
-      for (int i = te0; i < te1; ++i) {
-        const uint32_t key = cand_key[i];
-        cgt += key > tau ? 1 : 0;
-        ceq += key == tau ? 1 : 0;
-      }
-    } else {
-      for (int qi = tq0; qi < tq1; ++qi) {
-        uint4 k4 = make_uint4(0u, 0u, 0u, 0u);
-        if (!all) k4 = keys4[qi];
-        const uint32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int idx = qi * 4 + e;
-          const bool in = idx >= koff && idx < koff + nloc;
-          cgt += (in && (all || kv[e] > tau)) ? 1 : 0;
-          ceq += (in && !all && kv[e] == tau) ? 1 : 0;
-        }
-      }
+    for (int w = tw0; w < tw1; ++w) {
+      cgt += __popc(s_gt[w]);
+      ceq += __popc(s_eq[w]);
     }
     // packed block scan of (gt, eq) counts: both stay below 2^16 per CTA
     const unsigned packed = (unsigned)cgt | ((unsigned)ceq << 16);
@@ -449,51 +618,33 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
     const unsigned inc = (unsigned)block_inclusive_scan((int)packed, s_ws, &tot);
     const int ex_gt = (int)((inc - packed) & 0xffffu), ex_eq = (int)((inc - packed) >> 16);
     const int tot_gt = (int)((unsigned)tot & 0xffffu), tot_eq = (int)((unsigned)tot >> 16);
-    int eo = 0, so = 0;                         // ties and selections before this CTA
+    int eo = 0, so_r = 0;                       // ties and selections before this CTA
     if (CS > 1) {
       if (tid < CS) {
         cluster.map_shared_rank(s_cgt, tid)[crank] = tot_gt;
         cluster.map_shared_rank(s_ceq, tid)[crank] = tot_eq;
       }
       cluster.sync();
-      for (int c = 0; c < crank; ++c) { so += s_cgt[c]; eo += s_ceq[c]; }
-      so += min(max(k_rem, 0), eo);
+      for (int c = 0; c < crank; ++c) { so_r += s_cgt[c]; eo += s_ceq[c]; }
+      so_r += min(max(k_rem, 0), eo);
     }
-    const int sel_off = so;                     // this CTA's first rank
+    const int sel_off = so_r;                   // this CTA's first rank
     n_sel = tot_gt + min(max(k_rem - eo, 0), tot_eq);
     int er = eo + ex_eq;                        // tie rank of this thread's first equal key
-    int rank = so + ex_gt + min(max(k_rem - eo, 0), ex_eq);
-    const int out_base = p.canonical ? s_fpre : F;
-    long long* ro = p.rows_out ? p.rows_out + (size_t)seg * p.S + out_base : nullptr;
-    auto emit = [&](int idx) {
-      const long long row = seg_off + (long long)(kbase + idx - p.lo);
-      if (ro) ro[rank] = row;
-      s_arow[fshare + (rank - sel_off)] = checked_row(row, p.total_rows, p.err);
-      ++rank;
-    };
-    if (use_list) {
-      for (int i = te0; i < te1; ++i) {
-        const uint32_t key = cand_key[i];
-        if (key > tau) emit((int)cand_idx[i]);
-        else if (key == tau) {
-          if (er < k_rem) emit((int)cand_idx[i]);
-          ++er;
-        }
-      }
-    } else {
-      for (int qi = tq0; qi < tq1; ++qi) {
-        uint4 k4 = make_uint4(0u, 0u, 0u, 0u);
-        if (!all) k4 = keys4[qi];
-        const uint32_t kv[4] = {k4.x, k4.y, k4.z, k4.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int idx = qi * 4 + e;
-          if (!(idx >= koff && idx < koff + nloc)) continue;
-          if (all || kv[e] > tau) emit(idx);
-          else if (kv[e] == tau) {
-            if (er < k_rem) emit(idx);
-            ++er;
-          }
+    int rank = so_r + ex_gt + min(max(k_rem - eo, 0), ex_eq);
+    for (int w = tw0; w < tw1; ++w) {
+      const uint32_t gw = s_gt[w];
+      uint32_t m = gw | s_eq[w];
+      while (m) {
+        const int bit = __ffs(m) - 1;
+        m &= m - 1u;
+        bool take = true;
+        if (!((gw >> bit) & 1u)) take = er++ < k_rem;
+        if (take) {
+          const long long row = seg_off + (long long)(kb + 32 * w + bit - p.lo);
+          if (ro) ro[rank] = row;
+          s_arow[fshare + (rank - sel_off)] = checked_row(row, p.total_rows, p.err);
+          ++rank;
         }
       }
     }
@@ -504,10 +655,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
   if (p.rows_out && crank == 0 && tid < 32) {
     // F into the row list: first (reference order), or around the candidates when canonical
     const int lane = tid;
-    long long* ro = p.rows_out + (size_t)seg * p.S;
+    long long* rf = p.rows_out + (size_t)seg * p.S;
     const long long* fr = p.fixed_rows + (size_t)seg * F;
     if (!p.canonical) {
-      for (int i = lane; i < F; i += 32) ro[i] = fr[i];
+      for (int i = lane; i < F; i += 32) rf[i] = fr[i];
     } else {
       int nlo = 0, nhi = 0;
       const unsigned lt = (1u << lane) - 1u;
@@ -516,8 +667,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
         const long long v = i < F ? fr[i] : 0;
         const bool lo_side = i < F && v < seg_off, hi_side = i < F && v >= seg_off;
         const unsigned ml = __ballot_sync(0xffffffffu, lo_side), mh = __ballot_sync(0xffffffffu, hi_side);
-        if (lo_side) ro[nlo + __popc(ml & lt)] = v;
-        if (hi_side) ro[s_fpre + p.k + nhi + __popc(mh & lt)] = v;
+        if (lo_side) rf[nlo + __popc(ml & lt)] = v;
+        if (hi_side) rf[s_fpre + p.k + nhi + __popc(mh & lt)] = v;
         nlo += __popc(ml);
         nhi += __popc(mh);
       }

@@ -321,3 +321,32 @@ def test_ties_go_to_the_smaller_position_for_every_cluster_size(pattern):
         _, _, _, _, rows, _, _ = run_step(case, cluster=cl, t=t)
         got = rows.reshape(case.B, case.G, -1)[..., c["fixed_count"]:] - c["off_lo"] + c["lo"]
         assert np.array_equal(np.sort(got, axis=-1), np.sort(want, axis=-1)), f"cluster {cl}"
+
+
+@pytest.mark.parametrize("pattern", ["all_equal", "half_equal", "three_values"])
+def test_ties_with_candidate_list_overflow(pattern):
+    """60000 candidates with heavy ties: a CTA whose filtered candidate list overflows rescans the index columns
+    (clusters 1 and 2: one CTA holds more tied keys than its list), and in half_equal only the CTA over the tied
+    half overflows, so the cluster must agree on the rescan. The chosen set must still be the oracle's
+    (score desc, position asc) top-k."""
+    case = cs.Case("ties_large", G=2, h=2, C=60000, L=60000, kv_dtype="bfloat16", seed=21)
+    t = cs.build(case)
+    c = cs.step_constants(case)
+    zt = t["zT"]
+    n_cand = case.L - 1
+    if pattern == "all_equal":
+        zt[..., :n_cand] = zt[..., 100:101]
+    elif pattern == "half_equal":
+        zt[..., : n_cand // 2] = zt[..., 100:101]
+    else:
+        idx = torch.arange(n_cand) % 3
+        zt[..., :n_cand] = zt[..., 100:103][..., idx]
+    s64 = oracle_scores(t, c)
+    for cl in (1, 2, 4):
+        _, _, _, out, rows, _, scores = run_step(case, cluster=cl, t=t)
+        check_scores(scores, s64)
+        # exact top-k of the kernel's own fp32 scores under (score desc, position asc)
+        want = orc.topk_indices(scores.astype(np.float64), c["k"]) + c["lo"]
+        got = rows.reshape(case.B, case.G, -1)[..., c["fixed_count"]:] - c["off_lo"] + c["lo"]
+        assert np.array_equal(np.sort(got, axis=-1), np.sort(want, axis=-1)), f"cluster {cl}"
+        assert np.all(np.diff(got, axis=-1) > 0), "chosen candidates in ascending position order"
