@@ -54,6 +54,19 @@ SIGNATURES = {
                            c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p],
     "al_candidate_scores": [c_void_p, P64, c_void_p, c_int,
                             c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p],
+    "al_context_local_topk": [c_void_p, c_int64, c_int64, c_int64,
+                              c_void_p, c_void_p, c_void_p, c_int,
+                              c_void_p, c_int64, c_int64,
+                              c_void_p, c_void_p,
+                              c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                              c_int64, c_int, c_void_p, c_void_p, c_int, c_void_p],
+    "al_context_threshold": [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+                             c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "al_gathered_attend_partial": [c_void_p, c_int64, c_int64, c_int64,
+                                   c_void_p, c_void_p, c_int, c_void_p,
+                                   c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                   c_void_p, c_int, c_void_p],
+    "al_lse_merge": [c_void_p, c_int, c_int, c_int, c_int, c_int, c_void_p, c_int, c_void_p],
 }
 
 _lib = None

@@ -1,0 +1,149 @@
+"""Context split of one decode step across the ranks of a process group (config C4: one long sequence, one GPU per
+contiguous shard of its positions).
+
+attention-lab's decode step (decode.py:145-163) runs on one device. Split across P ranks, each rank holds positions
+[start, start + shard_capacity) of every cache (K, V, zT) and, per layer:
+
+    1. scores its own candidates and takes a local top-k (a 64-bit key per candidate: the score's order key above
+       the inverted position, so (score desc, position asc) is plain integer order and no two candidates tie);
+    2. all-gathers the keys (P * k * 8 bytes per (batch, group));
+    3. finds the global k-th key and keeps its candidates at or above it: exactly the single-device top-k set;
+    4. attends over F's rows on its shard plus its kept candidates into an unnormalised partial (m, l, acc);
+    5. all-gathers the partials (P * h * 130 floats per (batch, group)) and merges them by log-sum-exp.
+
+Every rank ends with the same output. F's prefix lives on the first shard, its recent window on the shard(s) that
+hold the last positions; the newest key's z column is written by the shard that owns position L - 1.
+
+The device work goes through an `ops` object (default: `CudaContextOps`, the sm_100a kernels). Tests hand the same
+orchestration CPU stand-ins to check the protocol over gloo ranks; the CUDA path itself has no CPU fallback.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+from . import ops as _ops
+from .selection import row_offsets, selection_layout
+
+SHARD_ALIGN = 16   # positions; keeps every shard's zT rows 16-byte aligned for the vector scan
+
+
+@dataclass(frozen=True)
+class ShardPlan:
+    """One rank's view of a decode step whose legal range is [0, legal_length)."""
+
+    rank: int
+    world: int
+    legal_length: int
+    k: int                      # global top-k size (selection.py rules)
+    start: int                  # global position of local column 0
+    shard_capacity: int         # positions held per rank
+    lo: int                     # local candidate columns [lo, hi)
+    hi: int
+    fixed_local: tuple          # local columns of F on this shard (global F order)
+    k_local: int                # min(k, hi - lo)
+
+    @property
+    def fixed_count(self) -> int:
+        return len(self.fixed_local)
+
+    @property
+    def selected_count(self) -> int:
+        return self.fixed_count + self.k_local
+
+    @property
+    def write_col(self) -> int:
+        """Local column of position legal_length - 1, or -1 when another shard owns it."""
+        c = self.legal_length - 1 - self.start
+        return c if 0 <= c < self.shard_capacity else -1
+
+    def fixed_rows(self, batch: int, groups: int, device) -> torch.Tensor:
+        off = row_offsets(batch, groups, self.shard_capacity, device)
+        pos = torch.tensor(self.fixed_local, dtype=torch.long, device=device).view(1, 1, -1)
+        return (pos + off).contiguous()
+
+    def off_lo(self, batch: int, groups: int, device) -> torch.Tensor:
+        return (row_offsets(batch, groups, self.shard_capacity, device) + self.lo).contiguous()
+
+
+def shard_capacity(capacity: int, world: int) -> int:
+    """Positions per rank: an equal, aligned share of the global capacity."""
+    if world < 1:
+        raise ValueError("world must be >= 1")
+    per = -(-capacity // world)
+    return -(-per // SHARD_ALIGN) * SHARD_ALIGN
+
+
+def plan_shard(legal_length: int, k0: int, rank: int, world: int, capacity: int) -> ShardPlan:
+    """The selection rules of selection.py:21-86 for the whole sequence, restricted to rank's shard."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside [0, {world})")
+    cs = shard_capacity(capacity, world)
+    if legal_length > cs * world:
+        raise ValueError(f"legal length {legal_length} exceeds the shards' capacity {cs * world}")
+    lay = selection_layout(legal_length)
+    k = lay.clamp_k(k0)
+    start, end = rank * cs, (rank + 1) * cs
+    lo = min(max(lay.candidate_lo, start), end) - start
+    hi = max(min(lay.candidate_hi, end), start) - start
+    hi = max(hi, lo)
+    fixed = tuple(p - start for p in lay.fixed_positions() if start <= p < end)
+    return ShardPlan(rank=rank, world=world, legal_length=int(legal_length), k=int(k), start=start,
+                     shard_capacity=cs, lo=lo, hi=hi, fixed_local=fixed, k_local=min(int(k), hi - lo))
+
+
+class CudaContextOps:
+    """The four device steps on the sm_100a kernels (C ABI entries al_context_local_topk, al_context_threshold,
+    al_gathered_attend_partial, al_lse_merge)."""
+
+    @staticmethod
+    def local_topk(q_pre, zT, wq_t_scaled, wk, plan: ShardPlan, *, k_pre_new=None):
+        B, G = q_pre.shape[:2]
+        dev = q_pre.device
+        return _ops.context_local_topk(q_pre, zT, wq_t_scaled, wk, plan.fixed_rows(B, G, dev), plan.off_lo(B, G, dev),
+                                       plan.lo, plan.hi, plan.k_local, key_pos=plan.start, key_stride=plan.k,
+                                       k_pre_new=k_pre_new, write_col=plan.write_col)
+
+    @staticmethod
+    def threshold(all_keys, rows, plan: ShardPlan):
+        return _ops.context_threshold(all_keys, rows, plan.rank, plan.k, plan.fixed_count, plan.k_local)
+
+    @staticmethod
+    def attend_partial(q_main, k_cache, v_cache, rows, scale):
+        return _ops.gathered_attend_partial(q_main, k_cache, v_cache, rows, scale=scale)
+
+    @staticmethod
+    def lse_merge(all_parts, dtype):
+        return _ops.lse_merge(all_parts, dtype)
+
+
+def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
+    buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
+    dist.all_gather(list(buf.unbind(0)), t.contiguous(), group=group)
+    return buf
+
+
+def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan: ShardPlan, *,
+                              group=None, k_pre_new=None, scale=None, ops=None):
+    """One layer's sparse decode step with the sequence split over the group's ranks (this rank holds the shard of
+    `plan`: caches [B,G,shard_capacity,d] and zT [B,G,r,shard_capacity]). Every rank calls it with the same global
+    step and gets the full output [B,G,h,1,d]; it equals decode.py:145-163 run on the unsplit caches."""
+    ops = CudaContextOps if ops is None else ops
+    world = plan.world
+    if dist.is_initialized() and dist.get_world_size(group) != world:
+        raise ValueError(f"plan is for {world} ranks, the group has {dist.get_world_size(group)}")
+    B, G, h, _, d = q_main.shape
+    if plan.selected_count > 0:
+        rows, keys = ops.local_topk(q_pre, zT, wq_t_scaled, wk, plan, k_pre_new=k_pre_new)
+    else:   # a shard past the legal range: nothing to score, nothing to attend
+        rows = torch.empty((B, G, 0), dtype=torch.int64, device=q_main.device)
+        keys = torch.zeros((B, G, plan.k), dtype=torch.int64, device=q_main.device)
+    if plan.k > 0:   # the same on every rank
+        all_keys = _all_gather(keys, world, group)
+        if plan.selected_count > 0:
+            rows = ops.threshold(all_keys, rows, plan)
+    part = ops.attend_partial(q_main, k_cache, v_cache, rows, scale)
+    all_parts = _all_gather(part, world, group)
+    return ops.lse_merge(all_parts, q_main.dtype)

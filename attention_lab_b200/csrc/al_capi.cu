@@ -7,7 +7,7 @@
 #include <mutex>
 #include <unordered_map>
 
-#include "al_decode.cuh"
+#include "al_context.cuh"
 #include "al_index.cuh"
 #include "../../include/attention_lab_b200.h"
 
@@ -233,7 +233,9 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
   if (p.k_new && !p.wk) return fail(AL_EINVAL, "k_pre_new given without wk");
 
   p.select_mode = p.k == 0 ? 0 : (p.k == p.M ? 2 : 1);
-  p.scan = (p.select_mode == 1 || p.scores_out) ? 1 : 0;
+  p.scan = (p.select_mode == 1 || p.scores_out || (p.keys_out && p.select_mode == 2)) ? 1 : 0;
+  if (p.keys_out && (p.kst < p.k || p.key_pos < 0 || p.key_pos + (long long)p.C > 0xffffffffLL))
+    return fail(AL_EINVAL, "key_stride=%d must be >= k=%d and key positions must fit 32 bits", p.kst, p.k);
   if (p.scan && !p.u_in && (!p.q_pre || !p.wq_t)) return fail(AL_EINVAL, "null q_pre or wq_t");
   const int ez = esize(idx_dtype);
   p.zvec = ((long long)p.C * ez % 16 == 0) && aligned16(p.zT) ? 1 : 0;
@@ -271,7 +273,11 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
         const size_t room = eng > sel_fixed ? (eng - sel_fixed) / 8 : 0;
         p.cap = (int)std::min<size_t>((size_t)p.cpc, std::max<size_t>(room, (size_t)cap_min));
       }
-      const size_t select_bytes = sel_fixed + (size_t)p.cap * 8;
+      size_t select_bytes = sel_fixed + (size_t)p.cap * 8;
+      if (p.keys_out) {                     // per-column keys of the chosen candidates
+        p.skey_off = (int)round_up(select_bytes, 16);
+        select_bytes = (size_t)p.skey_off + (size_t)(p.cpc + 64) * 4;
+      }
       p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
       smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
       p.nstage = st;
@@ -362,7 +368,7 @@ static int run_attend(AttendParams p, int kv_dtype, int d, int n_all, int cluste
   if (!p.q || !p.k_cache || !p.v_cache || (!p.out && !p.part)) return fail(AL_EINVAL, "null pointer argument");
   if (!aligned16(p.k_cache) || !aligned16(p.v_cache))
     return fail(AL_EUNSUPPORTED, "k_cache and v_cache must start on a 16-byte boundary");
-  if (n_all < 1) return fail(AL_EINVAL, "at least one row must be read");
+  if (n_all < (p.part ? 0 : 1)) return fail(AL_EINVAL, "at least one row must be read");
   const long long total = (long long)p.B * p.G * p.C;
   if (total >= 0xffffffffLL) return fail(AL_EUNSUPPORTED, "B*G*C exceeds 2^32-1 rows");
   p.total_rows = total;
@@ -373,7 +379,7 @@ static int run_attend(AttendParams p, int kv_dtype, int d, int n_all, int cluste
     while (cs < kMaxCluster && p.B * p.G * cs < di->sms && n_all / (cs * 2) >= 64) cs <<= 1;
   }
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
-  p.rows_cap = p.mode == 0 ? (n_all + cs - 1) / cs : 0;
+  p.rows_cap = p.mode == 0 ? std::max(1, (n_all + cs - 1) / cs) : 0;
   p.nstage = kStages;
   const size_t smem = (size_t)engine_smem(kv_dtype, hp) + (size_t)p.rows_cap * 4;
   if ((long long)smem > di->max_smem_optin - kAttendStaticBytes)
@@ -515,6 +521,80 @@ int al_candidate_scores(const void* u, const int64_t* u_strides, const void* zT,
   if (idx_dtype == AL_F32) candidate_scores_kernel<float><<<grid, kThreads, 0, st>>>(p);
   else candidate_scores_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(p);
   return plain_launch_check("candidate_scores_kernel");
+}
+
+
+int al_context_local_topk(const void* q_pre, int64_t qp_sb, int64_t qp_sg, int64_t qp_sh,
+                          void* zT, const void* wq_t, const void* wk, int idx_dtype,
+                          const void* k_pre_new, int64_t kn_sb, int64_t kn_sg,
+                          const int64_t* fixed_rows, const int64_t* off_lo,
+                          int B, int G, int h, int r, int C, int lo, int hi, int k, int fixed_count, int write_col,
+                          int64_t key_pos, int key_stride, int64_t* rows_out, uint64_t* keys_out, int cluster,
+                          void* stream) {
+  if (!rows_out || !keys_out) return fail(AL_EINVAL, "rows_out and keys_out are required");
+  DecodeParams p = {};
+  p.B = B; p.G = G; p.h = h; p.r = r; p.C = C;
+  p.lo = lo; p.hi = hi; p.k = k; p.S = fixed_count + k; p.F = fixed_count; p.write_col = write_col;
+  p.q_pre = q_pre; p.qp_sb = qp_sb; p.qp_sg = qp_sg; p.qp_sh = qp_sh;
+  p.wq_t = wq_t; p.wk = wk;
+  p.k_new = k_pre_new; p.kn_sb = kn_sb; p.kn_sg = kn_sg;
+  p.zT = zT;
+  p.fixed_rows = reinterpret_cast<const long long*>(fixed_rows);
+  p.off_lo = reinterpret_cast<const long long*>(off_lo);
+  p.rows_out = reinterpret_cast<long long*>(rows_out);
+  p.keys_out = reinterpret_cast<unsigned long long*>(keys_out);
+  p.key_pos = key_pos; p.kst = key_stride;
+  if (p.S < 1) return fail(AL_EINVAL, "a shard with no rows takes no part in the step (fixed_count + k == 0)");
+  return run_fused(p, AL_BF16, idx_dtype, kHeadDim, cluster, stream, false);
+}
+
+int al_context_threshold(const uint64_t* keys, int world, int rank, int B, int G, int key_stride, int k,
+                         int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend, void* stream) {
+  if (!keys || !rows_in || !rows_attend) return fail(AL_EINVAL, "null pointer argument");
+  if (world < 1 || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
+  if (B <= 0 || G <= 0 || B * (long long)G > 0x7fffffffLL) return fail(AL_EINVAL, "B and G must be positive");
+  if (k < 1 || key_stride < 1 || k > (long long)world * key_stride)
+    return fail(AL_EINVAL, "k=%d must lie in [1, world*key_stride=%lld]", k, (long long)world * key_stride);
+  if (k_local < 0 || k_local > key_stride || fixed_count < 0)
+    return fail(AL_EINVAL, "k_local=%d must lie in [0, key_stride=%d]", k_local, key_stride);
+  if (fixed_count + k_local == 0) return AL_OK;
+  CtxParams p = {};
+  p.P = world; p.B = B; p.G = G; p.kst = key_stride; p.k = k; p.rank = rank; p.F = fixed_count; p.k_local = k_local;
+  p.keys = reinterpret_cast<const unsigned long long*>(keys);
+  p.rows_in = reinterpret_cast<const long long*>(rows_in);
+  p.rows_attend = reinterpret_cast<long long*>(rows_attend);
+  context_threshold_kernel<<<B * G, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return plain_launch_check("context_threshold_kernel");
+}
+
+int al_gathered_attend_partial(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                               const void* k_cache, const void* v_cache, int kv_dtype, const int64_t* rows,
+                               int B, int G, int h, int d, int C, int n_rows, float scale,
+                               float* part, int cluster, void* stream) {
+  if ((!rows && n_rows > 0) || !part) return fail(AL_EINVAL, "null rows or part");
+  if (n_rows < 0) return fail(AL_EINVAL, "n_rows must be >= 0");
+  AttendParams p = {};
+  p.B = B; p.G = G; p.h = h; p.C = C; p.S = n_rows; p.mode = 0; p.skip_neg = 1;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.q = q_main; p.q_sb = q_sb; p.q_sg = q_sg; p.q_sh = q_sh;
+  p.k_cache = k_cache; p.v_cache = v_cache;
+  p.rows = reinterpret_cast<const long long*>(rows);
+  p.part = part;
+  return run_attend(p, kv_dtype, d, n_rows, n_rows == 0 ? 1 : cluster, stream);
+}
+
+int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void* out, int out_dtype, void* stream) {
+  if (!parts || !out) return fail(AL_EINVAL, "null pointer argument");
+  if (!dtype_ok(out_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (world < 1 || B <= 0 || G <= 0 || h <= 0) return fail(AL_EINVAL, "world, B, G and h must be positive");
+  const long long n = (long long)B * G * h;
+  if (n * kHeadDim > 0x7fffffffLL) return fail(AL_EUNSUPPORTED, "B*G*h too large");
+  const unsigned grid = (unsigned)((n * kHeadDim + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (out_dtype == AL_BF16) lse_merge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<__nv_bfloat16*>(out));
+  else lse_merge_kernel<float><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<float*>(out));
+  return plain_launch_check("lse_merge_kernel");
 }
 
 }  // extern "C"

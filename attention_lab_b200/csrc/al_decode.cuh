@@ -52,6 +52,10 @@ struct DecodeParams {
   float* part;                                      // [B,G,h,130] partial (m, l, acc) instead of out, nullable
   long long* rows_out;                              // [B,G,S], nullable
   float* scores_out;                                // [B,G,M], nullable
+  unsigned long long* keys_out;                     // [B,G,kst] 64-bit keys of the chosen candidates, nullable
+  long long key_pos;                                // position of column 0 in the keys (a shard's first position)
+  int kst;                                          // keys_out entries per segment (>= k; the rest are zero)
+  int skey_off;                                     // selection region: per-column keys (keys_out only)
   unsigned* err;                                    // device error word
 };
 
@@ -361,6 +365,7 @@ struct SinkRescan {
   bool marks;
   unsigned* hist; uint32_t prefix, pmask; int shift;
   uint32_t* gt; uint32_t* eq; uint32_t tau; int kb;
+  uint32_t* skey;                                            // per-column keys of the marked columns, nullable
   template <int VW>
   __device__ __forceinline__ void put(int col, const uint32_t* kk, const float*, unsigned vm) {
     if (!marks) {
@@ -379,9 +384,35 @@ struct SinkRescan {
     const int rel = col - kb;                                // a multiple of VW: the VW bits share one word
     if (gm) atomicOr(&gt[rel >> 5], gm << (rel & 31));
     if (em) atomicOr(&eq[rel >> 5], em << (rel & 31));
+    if (skey) {
+#pragma unroll
+      for (int e = 0; e < VW; ++e)
+        if (((gm | em) >> e) & 1u) skey[rel + e] = kk[e];
+    }
   }
   __device__ __forceinline__ void round_end(int) {}
 };
+
+// Every candidate chosen (k == M) but the keys requested: store every valid column's key.
+struct SinkKeys {
+  uint32_t* skey; int kb; float* so;
+  template <int VW>
+  __device__ __forceinline__ void put(int col, const uint32_t* kk, const float* sc, unsigned vm) {
+#pragma unroll
+    for (int e = 0; e < VW; ++e)
+      if ((vm >> e) & 1u) {
+        skey[col + e - kb] = kk[e];
+        if (so) so[col + e] = sc[e];
+      }
+  }
+  __device__ __forceinline__ void round_end(int) {}
+};
+
+// 64-bit candidate key: the score's order key above the inverted position, so a larger key ranks first under
+// (score desc, position asc) and no two positions tie.
+__device__ __forceinline__ unsigned long long pack_key64(uint32_t key, long long pos) {
+  return ((unsigned long long)key << 32) | (unsigned long long)(0xffffffffu - (uint32_t)pos);
+}
 
 // Scores only (no top-k): write the fp32 scores.
 struct SinkScores {
@@ -485,6 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
   const uint32_t* s_lkey = reinterpret_cast<const uint32_t*>(dsm + p.list_off);
   const uint32_t* s_lcol = s_lkey + p.cap;
   uint32_t* s_arow = reinterpret_cast<uint32_t*>(dsm + p.union_bytes);
+  uint32_t* s_skey = p.keys_out ? reinterpret_cast<uint32_t*>(dsm + p.skey_off) : nullptr;   // [column - kb]
 #define CSYNC() do { if (CS > 1) cluster.sync(); else __syncthreads(); } while (0)
 
   const int c0 = p.lo + crank * p.cpc;
@@ -513,6 +545,9 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
         SinkFirst<false> sk{nullptr, p.list_off, p.cap, p.k, kb};
         scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
       }
+    } else if (s_skey) {
+      SinkKeys sk{s_skey, kb, so};
+      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
     } else {
       SinkScores sk{so};
       scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
@@ -561,10 +596,11 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
           } else if (key >= prefix) {
             const uint32_t c = s_lcol[i];
             atomicOr(key > prefix ? &s_gt[c >> 5] : &s_eq[c >> 5], 1u << (c & 31));
+            if (s_skey) s_skey[c] = key;
           }
         }
       } else if (nloc > 0) {
-        SinkRescan sk{pass == 2, s_hist, prefix, pmask, shift, s_gt, s_eq, prefix, kb};
+        SinkRescan sk{pass == 2, s_hist, prefix, pmask, shift, s_gt, s_eq, prefix, kb, s_skey};
         scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
       }
       if (pass < 2) {
@@ -600,6 +636,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
     for (int c = c0 + tid; c < c1; c += kThreads) {
       const long long row = seg_off + (long long)(c - p.lo);
       if (ro) ro[c - p.lo] = row;
+      if (p.keys_out) p.keys_out[(size_t)seg * p.kst + (c - p.lo)] = pack_key64(s_skey[c - kb], p.key_pos + c);
       s_arow[fshare + (c - c0)] = checked_row(row, p.total_rows, p.err);
     }
   } else if (p.select_mode == 1) {
@@ -643,12 +680,16 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
         if (take) {
           const long long row = seg_off + (long long)(kb + 32 * w + bit - p.lo);
           if (ro) ro[rank] = row;
+          if (p.keys_out)
+            p.keys_out[(size_t)seg * p.kst + rank] = pack_key64(s_skey[32 * w + bit], p.key_pos + kb + 32 * w + bit);
           s_arow[fshare + (rank - sel_off)] = checked_row(row, p.total_rows, p.err);
           ++rank;
         }
       }
     }
   }
+  if (p.keys_out && crank == 0)
+    for (int i = p.k + tid; i < p.kst; i += kThreads) p.keys_out[(size_t)seg * p.kst + i] = 0ull;   // below every key
   for (int i = tid; i < fshare; i += kThreads)
     s_arow[i] = checked_row(p.fixed_rows[(size_t)seg * F + fsh0 + i], p.total_rows, p.err);
   __syncthreads();
@@ -695,6 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodePa
 struct AttendParams {
   int B, G, h, C, S, L;
   int mode;               // 0: gathered rows [B,G,S] flat ids; 1: dense range [0, L) of each segment
+  int skip_neg;           // mode 0: a negative row id marks a row that is not read (no error)
   int rows_cap;
   int nstage;             // attend pipeline depth (4..8)
   float scale_log2;
@@ -723,8 +765,10 @@ __global__ void __launch_bounds__(kThreads, 1) attend_kernel(const AttendParams 
   RowSrc rs{nullptr, 0u};
   if (p.mode == 0) {
     uint32_t* s_arow = reinterpret_cast<uint32_t*>(dsm + Cfg::smem(p.nstage));
-    for (int i = threadIdx.x; i < r1 - r0; i += kThreads)
-      s_arow[i] = checked_row(p.rows[(size_t)seg * p.S + r0 + i], p.total_rows, p.err);
+    for (int i = threadIdx.x; i < r1 - r0; i += kThreads) {
+      const long long row = p.rows[(size_t)seg * p.S + r0 + i];
+      s_arow[i] = (p.skip_neg && row < 0) ? 0xffffffffu : checked_row(row, p.total_rows, p.err);
+    }
     __syncthreads();
     rs.list = s_arow;
   } else {

@@ -308,3 +308,111 @@ def append_kvz(k_cache, v_cache, zT, start: int, k_new, v_new, z_new=None, *, k_
             k_cache.data_ptr(), v_cache.data_ptr(), kv, k_new.data_ptr(), _lib.strides(k_new, 4), v_new.data_ptr(),
             _lib.strides(v_new, 4), nd, _ptr(zT), idx, _ptr(z_new), zs, _ptr(k_pre), kps, _ptr(wk),
             B, G, C, d, r, int(start), T, _stream(dev)))
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# context split across ranks (config C4): the device steps driven by attention_lab_b200.context_split
+# ---------------------------------------------------------------------------------------------------------------------
+def context_local_topk(q_pre, zT, wq_t_scaled, wk, fixed_rows, off_lo, lo: int, hi: int, k: int, *, key_pos: int,
+                       key_stride: int, k_pre_new=None, write_col: int = -1, cluster: int = 0):
+    """Local top-k of one shard's candidates [lo, hi): returns (rows [B,G,F+k] int64: F then the chosen candidates in
+    ascending position order, as flat ids of the shard's cache; keys [B,G,key_stride] int64 holding the chosen
+    candidates' 64-bit keys (score order key << 32 | 2^32-1 - (key_pos + column)), zero past k). Writes z of the
+    newest key into zT[..., write_col] when k_pre_new is given."""
+    dev = _cuda(q_pre, zT, wq_t_scaled, wk, fixed_rows, off_lo, k_pre_new)
+    q_pre, psb, psg, psh = _q_strides(q_pre, "q_pre")
+    B, G, h, _, d = q_pre.shape
+    if zT.dim() != 4 or zT.shape[0] != B or zT.shape[1] != G or not zT.is_contiguous():
+        raise ValueError("zT must be a contiguous [B,G,r,C] tensor")
+    r, C = zT.shape[2], zT.shape[3]
+    idx = _code(zT, "zT")
+    for t, what in ((q_pre, "q_pre"), (wq_t_scaled, "wq_t_scaled"), (wk, "wk"), (k_pre_new, "k_pre_new")):
+        if t is not None and t.dtype != zT.dtype:
+            raise ValueError(f"{what} must have the index dtype {zT.dtype}, got {t.dtype}")
+    if tuple(wq_t_scaled.shape) != (G, h * d, r) or tuple(wk.shape) != (G, r, d):
+        raise ValueError("wq_t_scaled must be [G,h*d,r] and wk [G,r,d]")
+    wq_t_scaled, wk = wq_t_scaled.contiguous(), wk.contiguous()
+    F = int(fixed_rows.shape[-1])
+    if tuple(fixed_rows.shape) != (B, G, F) or fixed_rows.dtype != torch.int64:
+        raise ValueError("fixed_rows must be int64 [B,G,F]")
+    if off_lo.numel() != B * G or off_lo.dtype != torch.int64:
+        raise ValueError("off_lo must be int64 [B,G,1]")
+    fixed_rows, off_lo = fixed_rows.contiguous(), off_lo.contiguous()
+    kn_sb = kn_sg = 0
+    if k_pre_new is not None:
+        if tuple(k_pre_new.shape) != (B, G, 1, d):
+            raise ValueError("k_pre_new must be [B,G,1,d]")
+        if k_pre_new.stride(3) != 1:
+            k_pre_new = k_pre_new.contiguous()
+        kn_sb, kn_sg = k_pre_new.stride(0), k_pre_new.stride(1)
+    rows = torch.empty((B, G, F + k), dtype=torch.int64, device=dev)
+    keys = torch.empty((B, G, key_stride), dtype=torch.int64, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.al_context_local_topk(
+            q_pre.data_ptr(), psb, psg, psh, zT.data_ptr(), wq_t_scaled.data_ptr(), wk.data_ptr(), idx,
+            _ptr(k_pre_new), kn_sb, kn_sg, fixed_rows.data_ptr(), off_lo.data_ptr(),
+            B, G, h, r, C, int(lo), int(hi), int(k), F, int(write_col), int(key_pos), int(key_stride),
+            rows.data_ptr(), keys.data_ptr(), int(cluster), _stream(dev)))
+    return rows, keys
+
+
+def context_threshold(all_keys, rows, rank: int, k: int, fixed_count: int, k_local: int):
+    """rows [B,G,F+k_local] of rank with -1 in place of every candidate below the global k-th key of all_keys
+    [world,B,G,key_stride] (every rank's keys from context_local_topk)."""
+    dev = _cuda(all_keys, rows)
+    if all_keys.dim() != 4 or all_keys.dtype != torch.int64 or not all_keys.is_contiguous():
+        raise ValueError("all_keys must be a contiguous int64 [world,B,G,key_stride] tensor")
+    world, B, G, kst = all_keys.shape
+    if tuple(rows.shape) != (B, G, fixed_count + k_local) or rows.dtype != torch.int64:
+        raise ValueError("rows must be int64 [B,G,fixed_count+k_local]")
+    rows = rows.contiguous()
+    out = torch.empty_like(rows)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.al_context_threshold(all_keys.data_ptr(), world, int(rank), B, G, kst, int(k),
+                                            int(fixed_count), int(k_local), rows.data_ptr(), out.data_ptr(),
+                                            _stream(dev)))
+    return out
+
+
+def gathered_attend_partial(q_main, k_cache, v_cache, rows, *, scale=None, cluster: int = 0):
+    """Unnormalised attention partial over rows [B,G,n] (flat ids of the cache, -1 = not read): returns float32
+    [B,G,h,130] = (m in the log2 domain, l, acc[128]) per head, for lse_merge."""
+    dev = _cuda(q_main, k_cache, v_cache, rows)
+    q_main, qsb, qsg, qsh = _q_strides(q_main, "q_main")
+    B, G, h, _, d = q_main.shape
+    _check_cache(k_cache, "k_cache")
+    _check_cache(v_cache, "v_cache")
+    if k_cache.shape != v_cache.shape or k_cache.shape[0] != B or k_cache.shape[1] != G or k_cache.shape[3] != d:
+        raise ValueError(f"shape mismatch: q {tuple(q_main.shape)} k {tuple(k_cache.shape)} v {tuple(v_cache.shape)}")
+    kv = _code(q_main, "q_main")
+    if k_cache.dtype != q_main.dtype or v_cache.dtype != q_main.dtype:
+        raise ValueError("q_main, k_cache and v_cache must share one dtype")
+    if rows.dtype != torch.int64 or rows.numel() % (B * G) != 0:
+        raise ValueError("rows must be int64 with B*G*n elements")
+    n = rows.numel() // (B * G)
+    rows = rows.contiguous()
+    part = torch.empty((B, G, h, d + 2), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.al_gathered_attend_partial(
+            q_main.data_ptr(), qsb, qsg, qsh, k_cache.data_ptr(), v_cache.data_ptr(), kv, rows.data_ptr(),
+            B, G, h, d, k_cache.shape[2], n, _scale(d, scale), part.data_ptr(), int(cluster), _stream(dev)))
+    return part
+
+
+def lse_merge(all_parts, dtype=torch.bfloat16):
+    """Merge partials [world,B,G,h,130] by log-sum-exp into out [B,G,h,1,d] of dtype."""
+    dev = _cuda(all_parts)
+    if all_parts.dim() != 5 or all_parts.dtype != torch.float32 or not all_parts.is_contiguous():
+        raise ValueError("all_parts must be a contiguous float32 [world,B,G,h,d+2] tensor")
+    world, B, G, h, d2 = all_parts.shape
+    out = torch.empty((B, G, h, 1, d2 - 2), dtype=dtype, device=dev)
+    code = _DTYPES.get(dtype)
+    if code is None:
+        raise ValueError(f"dtype must be float32 or bfloat16, got {dtype}")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        _lib.check(lib.al_lse_merge(all_parts.data_ptr(), world, B, G, h, d2 - 2, out.data_ptr(), code, _stream(dev)))
+    return out

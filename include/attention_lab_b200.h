@@ -110,6 +110,41 @@ int al_project_queries(const void* q_pre, const int64_t* qp_strides, const void*
 int al_candidate_scores(const void* u, const int64_t* u_strides, const void* zT, int idx_dtype,
                         int B, int G, int T, int r, int C, int lo, int hi, void* out, int out_f32, void* stream);
 
+/* ---- context split across GPUs (config C4; the multi-GPU protocol of the path, no single reference function):
+ * positions [0, L) are split into P contiguous shards, one per rank. Per layer: al_context_local_topk on every rank,
+ * an all-gather of the keys, al_context_threshold, al_gathered_attend_partial, an all-gather of the partials and
+ * al_lse_merge. The chosen set equals the single-device top-k of decode.py:92 exactly. */
+
+/* e1: local top-k of one shard (the select half of decode.py:145-163 on the shard's candidates [lo, hi)): writes the
+ *   z column (k_pre_new, when this shard owns write_col), rows_out [B,G,fixed_count+k] (F, then the chosen
+ *   candidates in ascending position order, as flat ids of the shard's cache) and keys_out [B,G,key_stride]: the
+ *   64-bit key of every chosen candidate in the same order ((score order key << 32) | (2^32-1 - position), position
+ *   = key_pos + column), zero past k. fixed_count + k must be >= 1. */
+int al_context_local_topk(const void* q_pre, int64_t qp_sb, int64_t qp_sg, int64_t qp_sh,
+                          void* zT, const void* wq_t, const void* wk, int idx_dtype,
+                          const void* k_pre_new, int64_t kn_sb, int64_t kn_sg,
+                          const int64_t* fixed_rows, const int64_t* off_lo,
+                          int B, int G, int h, int r, int C, int lo, int hi, int k, int fixed_count, int write_col,
+                          int64_t key_pos, int key_stride, int64_t* rows_out, uint64_t* keys_out, int cluster,
+                          void* stream);
+
+/* e2: global threshold: keys [world,B,G,key_stride] (every rank's keys_out) give the k-th largest key of each
+ *   segment; rows_attend [B,G,fixed_count+k_local] = rows_in (this rank's rows_out) with -1 in place of every
+ *   candidate below it. */
+int al_context_threshold(const uint64_t* keys, int world, int rank, int B, int G, int key_stride, int k,
+                         int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend, void* stream);
+
+/* e3: partial attention over rows [B,G,n_rows] (flat ids, -1 = not read) of the shard's cache (decode.py:131-142
+ *   without the final normalisation): part [B,G,h,130] = (m in the log2 domain, l, unnormalised acc[128]). */
+int al_gathered_attend_partial(const void* q_main, int64_t q_sb, int64_t q_sg, int64_t q_sh,
+                               const void* k_cache, const void* v_cache, int kv_dtype, const int64_t* rows,
+                               int B, int G, int h, int d, int C, int n_rows, float scale,
+                               float* part, int cluster, void* stream);
+
+/* e4: log-sum-exp merge of world partials [world,B,G,h,130] into out [B,G,h,d] (dtype out_dtype): the combine of
+ *   the reference's partitioned attend, metal_attend.py:147-169. */
+int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
