@@ -120,6 +120,8 @@ class CudaContextOps:
 
 
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
+    if world == 1:
+        return t.unsqueeze(0).contiguous()
     buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
     dist.all_gather(list(buf.unbind(0)), t.contiguous(), group=group)
     return buf
@@ -132,7 +134,7 @@ def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, 
     step and gets the full output [B,G,h,1,d]; it equals decode.py:145-163 run on the unsplit caches."""
     ops = CudaContextOps if ops is None else ops
     world = plan.world
-    if dist.is_initialized() and dist.get_world_size(group) != world:
+    if world > 1 and dist.get_world_size(group) != world:
         raise ValueError(f"plan is for {world} ranks, the group has {dist.get_world_size(group)}")
     B, G, h, _, d = q_main.shape
     if plan.selected_count > 0:

@@ -1,15 +1,15 @@
 // Gather-free attention engine: one CTA attends its h query heads over a list of K/V rows read in place.
 //
 // Rows are flat ids into the flattened [B*G*C, d] cache (the reference's row-id convention, sparse.py:14-16).
-// The engine streams the listed rows through shared memory with a multi-stage cp.async pipeline (16-byte chunks, a
-// bf16 row is 16 threads x 16 B; 4 to 8 stages of 64 rows, as shared memory allows), in three steps per chunk of up
-// to 1024 rows. (One-dimensional bulk copies, one per 256-byte row, measured about 2.5x slower on B200: the copy
-// engine's per-request cost dominates at this row size.)
-//   K sweep  - 16 lanes per row, 8 dims per lane; the h partial dot products are reduced across the 16 lanes with a
-//              transposed butterfly (5 shuffles for 4 heads) and the scores stored in shared memory;
-//   p pass   - the chunk's exact per-head maximum rescales the running state once, then p = exp2(s - m) is computed
-//              once per (row, head) in place and summed into l;
-//   V sweep  - acc += p * v with the same 16-lane layout.
+// The engine streams the listed rows through shared memory with a 3- to 5-stage cp.async pipeline of 32 KB tiles
+// (128 bf16 or 64 fp32 rows; 16-byte chunks XOR-swizzled by row), one continuous tile stream across sweeps and
+// chunks. Per chunk of up to CHUNK rows:
+//   K tiles  - the scores of every (row, head): tensor cores for bf16 rows (mma.sync m16n8k16, the tile's rows as
+//              A, the heads padded to 8 as B), CUDA cores for fp32 rows; stored head-major in shared memory;
+//   chunk end - the chunk's exact per-head maximum rescales the running state once, then p = exp2(s - m) is
+//              computed once per (row, head) (for bf16 rows rewritten in place as packed hi/lo bf16 fragments);
+//   V tiles  - acc += p * v: tensor cores for bf16 rows (O^T = V^T P^T, two MMAs per step for p's hi and lo
+//              halves), paired fp32 FMAs for fp32 rows.
 // No per-row rescale is needed. The result is the CTA's unnormalised partial (m, l, acc) per head in the log2
 // domain, merged across a thread-block cluster by `finish_output`.
 #pragma once
@@ -30,15 +30,17 @@ struct AttendCfg {
   static constexpr int KCH = NCH / KPARTS;                // K sweep: chunks per thread (4)
   static constexpr int LG = kThreads / 16;                // V sweep: 16-lane row groups per CTA
   static constexpr int RPG = TR / LG;                     // V sweep: rows per row group per tile
-  static constexpr int CHUNK = 2048;                      // rows scored before their V sweep
+  static constexpr int CHUNK = 512;                       // rows scored before their V sweep
   static constexpr int STAGE_BYTES = TR * ROWB;
   static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4;
   static_assert(RED_BYTES <= MIN_STAGES * STAGE_BYTES, "warp reduction buffer aliases the stage buffers");
   static_assert(RPG >= 1 && TR % LG == 0 && KCH * KPARTS == NCH && KPARTS * TR == kThreads, "tile shape");
   static_assert(CHUNK % TR == 0, "chunks hold whole tiles");
-  // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | K partial sums |
-  // q (pre-scaled) | warp maxima and sums
-  static constexpr int TAIL = CHUNK * HP * 4 + KPARTS * TR * HP * 4 + HP * kHeadDim * 4 + 2 * kWarps * HP * 4;
+  static_assert(kWarps % 8 == 0 && TR % (16 * (kWarps / 8)) == 0, "V tile: 8 warps over the dims, the rest over rows");
+  // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | warp maxima and sums |
+  // fp32 rows only: K partial sums, q. (bf16 rows keep q in registers; it is staged in the last stage buffer.)
+  static constexpr bool F32 = sizeof(KV_T) == 4;
+  static constexpr int TAIL = CHUNK * HP * 4 + 2 * kWarps * HP * 4 + (F32 ? KPARTS * TR * HP * 4 + HP * kHeadDim * 4 : 0);
   static constexpr __host__ __device__ int smem(int stages) { return stages * STAGE_BYTES + TAIL; }
   static constexpr int SMEM = MIN_STAGES * STAGE_BYTES + TAIL;
   // a staged row holds its 16-byte chunks XOR-swizzled by the row index, so both sweeps read without bank conflicts
@@ -116,9 +118,9 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
   const int krow = tid % Cfg::TR, kpart = tid / Cfg::TR; // K sweep row and dim part
   unsigned char* stages = dsm;
   float* s_sc = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES);
-  float* s_kp = s_sc + Cfg::CHUNK * HP;                  // [KPARTS][TR][HP] partial dot products
-  float* s_wm = s_kp + Cfg::KPARTS * Cfg::TR * HP + HP * kHeadDim;   // [kWarps][HP] warp maxima
+  float* s_wm = s_sc + Cfg::CHUNK * HP;                  // [kWarps][HP] warp maxima
   float* s_wl = s_wm + kWarps * HP;                      // [kWarps][HP] warp sums of p
+  float* s_kp = s_wl + kWarps * HP;                      // fp32 rows: [KPARTS][TR][HP] partial dot products
   const unsigned char* Kb = reinterpret_cast<const unsigned char*>(Kf);
   const unsigned char* Vb = reinterpret_cast<const unsigned char*>(Vf);
 
@@ -354,14 +356,15 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
       // ---------------- V tile: O += p * v ----------------
       if constexpr (sizeof(KV_T) == 2) {
         // tensor cores: O^T[dims x heads] += V^T[dims x rows] * P^T[rows x heads]. Warp w owns dims
-        // [16 (w & 7), +16) and the tile's rows [64 (w >> 3), +64) (4 steps of 16). Each p is split into a bf16 high
+        // [16 (w % 8), +16) and the tile's rows [RPW (w / 8), +RPW) in steps of 16. Each p is split into a bf16 high
         // part and a bf16 remainder (two MMAs), so p keeps about 16 mantissa bits; V is exact in bf16.
+        constexpr int RPW = Cfg::TR / (kWarps / 8);       // rows per warp
         const int mb = w & 7, khalf = w >> 3;
         const int g = lane >> 2, t4 = lane & 3;
         const int vr_lane = (lane & 7) + ((lane >> 4) << 3), vc_lane = 2 * mb + ((lane >> 3) & 1);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int r16 = 64 * khalf + 16 * kk;           // first row of this step within the tile
+        for (int kk = 0; kk < RPW / 16; ++kk) {
+          const int r16 = RPW * khalf + 16 * kk;          // first row of this step within the tile
           const int vr = r16 + vr_lane;
           uint32_t a0, a1, a2, a3;
           ldmatrix_x4_trans(smem_addr(buf + vr * Cfg::ROWB + Cfg::swz(vr, vc_lane) * 16), a0, a1, a2, a3);
@@ -407,7 +410,8 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
   // ---------------- CTA reduction ----------------
   float* red = reinterpret_cast<float*>(stages);
   if constexpr (sizeof(KV_T) == 2) {
-    // bf16 rows: red[khalf][head][128] from the O^T fragments, then the two row halves are added
+    // bf16 rows: red[row part][head][128] from the O^T fragments, then the row parts are added
+    constexpr int KH = kWarps / 8;
     const int mb = w & 7, khalf = w >> 3, g = lane >> 2, t4 = lane & 3;
 #pragma unroll
     for (int x = 0; x < 4; ++x) {
@@ -415,7 +419,12 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
       if (head < HP) red[(khalf * HP + head) * kHeadDim + dim] = oc[x];
     }
     __syncthreads();
-    for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) s_acc[idx] = red[idx] + red[HP * kHeadDim + idx];
+    for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) {
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < KH; ++i) a += red[i * HP * kHeadDim + idx];
+      s_acc[idx] = a;
+    }
   } else {
     // fp32 rows: 2 row groups per warp, then the warps
 #pragma unroll
@@ -489,13 +498,16 @@ __device__ void finish_output(KV_T* __restrict__ out, float* __restrict__ part, 
   if (CS > 1) cluster.sync();   // peers keep their shared memory alive until rank 0 has read it
 }
 
-// Write the heads' q into the engine's shared q buffer (HP x 128 floats; heads >= h are zero). Scores are scaled by
+// Write the heads' q into the engine's shared q buffer (HP x 128 floats; heads >= h are zero; for bf16 rows the
+// buffer is the last stage, which attend_rows reads before its first copy into that stage). Scores are scaled by
 // scale*log2 e after the dot products. Must be followed by a __syncthreads() before attend_rows reads it.
 template <typename KV_T, int HP>
 __device__ __forceinline__ float* stage_q(unsigned char* dsm, int nstage, const KV_T* __restrict__ qb, long long sh,
                                           int h) {
   using Cfg = AttendCfg<KV_T, HP>;
-  float* s_q = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::CHUNK * HP + Cfg::KPARTS * Cfg::TR * HP;
+  float* s_q = Cfg::F32 ? reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::CHUNK * HP + 2 * kWarps * HP +
+                              Cfg::KPARTS * Cfg::TR * HP
+                        : reinterpret_cast<float*>(dsm + (nstage - 1) * Cfg::STAGE_BYTES);
   for (int i = threadIdx.x; i < HP * kHeadDim; i += kThreads) {
     const int hh = i / kHeadDim, d = i % kHeadDim;
     s_q[i] = hh < h ? tof(qb[hh * sh + d]) : 0.f;

@@ -76,6 +76,8 @@ int prepare_kernel(K kernel, size_t smem, int cs) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(non-portable cluster)");
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(shared memory carve-out)");
     g_smem_set[key] = (int)smem;
   }
   (void)cs;
@@ -141,9 +143,9 @@ size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 constexpr int kFusedStaticBytes = 8 * 1024;
 constexpr int kAttendStaticBytes = 4 * 1024;
 
-constexpr int kStages = 5;   // deepest attend pipeline (32 KB stages); registers limit a 512-thread CTA to one per SM
-// The fused kernel keeps three stages: its selection code spills to local memory, and the L1 left beside a smaller
-// shared-memory carve-out holds those spills (measured: scan and selection faster, attend no slower than at five).
+// Attend pipeline depth (32 KB stages). Three stages keep a CTA of the fused or the attend kernel within half of an
+// SM's shared memory, so two 256-thread CTAs share each SM and one's selection or attend overlaps the other's scan.
+constexpr int kStages = 3;
 constexpr int kFusedStages = 3;
 
 int engine_smem(int kv_dtype, int hp, int stages = kStages) {

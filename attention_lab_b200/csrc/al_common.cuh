@@ -8,7 +8,7 @@
 namespace al {
 namespace cg = cooperative_groups;
 
-constexpr int kThreads = 512;              // threads per CTA for every decode kernel
+constexpr int kThreads = 256;              // threads per CTA for every decode kernel (two CTAs per SM)
 constexpr int kWarps = kThreads / 32;
 constexpr int kHeadDim = 128;              // d: 16 lanes x 8 dims per K/V row
 constexpr int kMaxR = 32;                  // index width r

@@ -128,19 +128,18 @@ __device__ void compute_u(const DecodeParams& p, int b, int g, float* s_u, float
 // z of the newest key: zT[b,g,j,write_col] = sum_e wk[g,j,e] * k_new[b,g,e], rounded to the index dtype.
 template <typename IDX_T>
 __device__ void write_z_column(const DecodeParams& p, int b, int g) {
-  static_assert(kThreads == 16 * kMaxR, "one 16-lane group per index row");
-  const int tid = threadIdx.x, j = tid >> 4, part = tid & 15, seg = b * p.G + g;
+  static_assert(kThreads == 8 * kMaxR, "one 8-lane group per index row");
+  const int tid = threadIdx.x, j = tid >> 3, part = tid & 7, seg = b * p.G + g;
   const IDX_T* kn = reinterpret_cast<const IDX_T*>(p.k_new) + b * p.kn_sb + g * p.kn_sg;
   const IDX_T* wk = reinterpret_cast<const IDX_T*>(p.wk) + ((size_t)g * p.r + (j < p.r ? j : 0)) * kHeadDim;
   float acc = 0.f;
   if (j < p.r) {
 #pragma unroll
-    for (int e = part * 8; e < part * 8 + 8; ++e) acc = fmaf(tof(wk[e]), tof(kn[e]), acc);
+    for (int e = part * 16; e < part * 16 + 16; ++e) acc = fmaf(tof(wk[e]), tof(kn[e]), acc);
   }
   acc += __shfl_xor_sync(0xffffffffu, acc, 1);
   acc += __shfl_xor_sync(0xffffffffu, acc, 2);
   acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 8);
   if (j < p.r && part == 0)
     reinterpret_cast<IDX_T*>(p.zT)[((size_t)seg * p.r + j) * p.C + p.write_col] = fromf<IDX_T>(acc);
 }
@@ -148,11 +147,9 @@ __device__ void write_z_column(const DecodeParams& p, int b, int g) {
 // Scores of candidate columns [c0, c1) -> order keys, handed to a sink. The scan runs in rounds of kThreads column
 // groups; every lane of every warp calls sink.put<VW>(col, keys, scores, mask) once per round (warp-convergent: the
 // sink may use warp collectives) with VW adjacent columns starting at `col` (bit e of `mask`: column col + e lies
-// in [c0, c1)), then sink.round_end(round). The scan is a call of its own so that its loads in flight get the
-// registers they need whatever the rest of the kernel holds (the caller saves its live values once). Recomputing a
-// column gives the same key bit for bit (same loads, same fused multiply-add order), so a sink may rescan. Vector
-// path: each thread owns VW adjacent columns and streams all r rows of them with 16-byte loads; u is read from
-// shared memory as broadcast float4s.
+// in [c0, c1)), then sink.round_end(round). Recomputing a column gives the same key bit for bit (same loads, same
+// fused multiply-add order), so a sink may rescan. Vector path: each thread owns VW adjacent columns and streams all
+// r rows of them with 16-byte loads; u is read from shared memory as broadcast float4s.
 struct ZSrc {                                              // a segment's index columns zT[b, g] ([r, C])
   const void* z; int r, C, vec;                            // vec: 16-byte aligned rows
 };
@@ -187,7 +184,7 @@ __device__ __forceinline__ void fma_rows8(float2 (&acc2)[V16<IDX_T>::n / 2], con
 }
 
 template <typename IDX_T, bool FULLR, typename Sink>
-__device__ __noinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1, const float* s_u, Sink sink) {
+__device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1, const float* s_u, Sink sink) {
   const IDX_T* zseg = reinterpret_cast<const IDX_T*>(zs.z);
   const int r = FULLR ? kMaxR : zs.r, C = zs.C;
   if (zs.vec) {
@@ -489,7 +486,7 @@ __device__ void pivot_round(cg::cluster_group& cluster, int CS, int crank, const
 }
 
 template <typename KV_T, typename IDX_T, int HP>
-__global__ void __launch_bounds__(kThreads, 1) sparse_step_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodeParams p) {
   unsigned char* dsm = g_dsm;
   __shared__ __align__(16) float s_u[kMaxR];
   __shared__ float s_pre[kWarps * 32];
@@ -750,7 +747,7 @@ struct AttendParams {
 };
 
 template <typename KV_T, int HP>
-__global__ void __launch_bounds__(kThreads, 1) attend_kernel(const AttendParams p) {
+__global__ void __launch_bounds__(kThreads, 2) attend_kernel(const AttendParams p) {
   using Cfg = AttendCfg<KV_T, HP>;
   extern __shared__ __align__(128) unsigned char dsm[];
   __shared__ float s_m[HP], s_l[HP];

@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU work budget of the CPU baseline sample")
     ap.add_argument("--batch", type=int, default=0, help="override the workload's requests per GPU (profiling cases)")
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling cases)")
+    ap.add_argument("--context-split", action="store_true",
+                    help="C4 measurement: one sequence split over the torchrun ranks (attention_lab_b200.context_split)")
     return ap.parse_args()
 
 
@@ -218,10 +220,77 @@ def config_of(args, desc, B, G, h, L, rho, layers):
 
 
 # ------------------------------------------------------------------------------------------------ GPU side
+def run_context_split(args):
+    """One layer of C4 (B=1, L=131072, rho=1/32) with its positions split over the torchrun ranks: every timed step is
+    the whole protocol (local top-k, key all-gather, threshold, partial attend, partial all-gather, merge). Device
+    time per step with CUDA events, max over ranks; prints one JSON line (rank 0)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from attention_lab_b200 import context_split as csplit
+    from attention_lab_b200.selection import fixed_budget
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _, B, G, h, L, rho, desc = WORKLOADS["c4"]
+    k0 = fixed_budget(L, rho)
+    plan = csplit.plan_shard(L, k0, rank, world, L)
+    cs_ = plan.shard_capacity
+    gen = torch.Generator(device=dev).manual_seed(99 + rank)
+
+    def rnd(*shape, scale=1.0):
+        t = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+        return t.normal_(0.0, scale, generator=gen)
+    K, V, Z = rnd(B, G, cs_, D), rnd(B, G, cs_, D), rnd(B, G, R, cs_, scale=0.23)
+    WQ, WK = rnd(G, h * D, R, scale=0.02 / math.sqrt(R)), rnd(G, R, D, scale=0.02)
+    Q, QP, KPN = rnd(B, G, h, 1, D), rnd(B, G, h, 1, D), rnd(B, G, 1, D)
+    kpn = KPN if plan.write_col >= 0 else None
+
+    def step():
+        return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=kpn)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    lg = ledger(B, G, h, L, rho, 1, 2, 2)
+    peak, _ = measured_peak()
+    if rank == 0:
+        print(json.dumps({"metric": "C4 context-split layer latency (whole protocol, max over ranks)",
+                          "value": round(ms * 1e3, 2), "unit": "us", "n_gpus": world, "steps": args.steps,
+                          "warmup": max(3, args.warmup), "higher_is_better": False, "scaling": "strong",
+                          "dtype": "bf16", "data": "synthetic",
+                          "config": {"workload": desc + f", split over {world} rank(s)", "k": lg["k"], "S": lg["S"],
+                                     "shard_capacity": cs_},
+                          "ledger_bytes": lg["d_s1_per_layer_request"],
+                          "achieved_gbs_aggregate": round(lg["d_s1_per_layer_request"] / (ms * 1e-3) / 1e9, 1),
+                          "peak_gbs_per_gpu": peak}))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.context_split:
+        return run_context_split(args)
     import torch
     import torch.distributed as dist
     import attention_lab_b200 as al
