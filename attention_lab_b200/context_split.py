@@ -19,7 +19,7 @@ orchestration CPU stand-ins to check the protocol over gloo ranks; the CUDA path
 """
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import torch
 import torch.distributed as dist
@@ -44,6 +44,7 @@ class ShardPlan:
     hi: int
     fixed_local: tuple          # local columns of F on this shard (global F order)
     k_local: int                # min(k, hi - lo)
+    _dev: dict = field(default_factory=dict, compare=False, repr=False)   # device tensors, built once per shape
 
     @property
     def fixed_count(self) -> int:
@@ -60,12 +61,18 @@ class ShardPlan:
         return c if 0 <= c < self.shard_capacity else -1
 
     def fixed_rows(self, batch: int, groups: int, device) -> torch.Tensor:
-        off = row_offsets(batch, groups, self.shard_capacity, device)
-        pos = torch.tensor(self.fixed_local, dtype=torch.long, device=device).view(1, 1, -1)
-        return (pos + off).contiguous()
+        key = ("fixed", batch, groups, str(device))
+        if key not in self._dev:
+            off = row_offsets(batch, groups, self.shard_capacity, device)
+            pos = torch.tensor(self.fixed_local, dtype=torch.long, device=device).view(1, 1, -1)
+            self._dev[key] = (pos + off).contiguous()
+        return self._dev[key]
 
     def off_lo(self, batch: int, groups: int, device) -> torch.Tensor:
-        return (row_offsets(batch, groups, self.shard_capacity, device) + self.lo).contiguous()
+        key = ("off_lo", batch, groups, str(device))
+        if key not in self._dev:
+            self._dev[key] = (row_offsets(batch, groups, self.shard_capacity, device) + self.lo).contiguous()
+        return self._dev[key]
 
 
 def shard_capacity(capacity: int, world: int) -> int:

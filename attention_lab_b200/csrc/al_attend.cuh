@@ -126,7 +126,9 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 
   float m_run[HP], l_run[HP];
   float2 acc[HP][4];                                    // fp32 rows: this lane's 8 dims per head
-  float oc[4] = {0.f, 0.f, 0.f, 0.f};                   // bf16 rows: O^T fragment (dims 16 (w & 7) + .., heads)
+  // bf16 rows: O^T fragment (dims 16 (w & 7) + .., heads), as four independent accumulators (p's hi and lo parts
+  // x even and odd row steps) so consecutive MMAs do not wait on each other; summed at the end
+  float oc[4][4] = {};
 #pragma unroll
   for (int hh = 0; hh < HP; ++hh) {
     m_run[hh] = -INFINITY;
@@ -205,13 +207,14 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
         if (w < Cfg::TR / 16) {
           const int lr = 16 * w + (lane & 15), lhi = lane >> 4;
           const uint32_t rowaddr = smem_addr(buf + lr * Cfg::ROWB);
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};   // even / odd dim steps
 #pragma unroll
           for (int ks = 0; ks < 8; ++ks) {
             uint32_t a0, a1, a2, a3;
             ldmatrix_x4(rowaddr + (uint32_t)(Cfg::swz(lr, 2 * ks + lhi) << 4), a0, a1, a2, a3);
-            mma_bf16_16816(c, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
+            mma_bf16_16816((ks & 1) ? co : ce, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
           }
+          const float c[4] = {ce[0] + co[0], ce[1] + co[1], ce[2] + co[2], ce[3] + co[3]};
           // c0, c1: row 16w + g, heads 2 t4, 2 t4 + 1; c2, c3: row 16w + g + 8
           const int g = lane >> 2, t4 = lane & 3;
 #pragma unroll
@@ -306,8 +309,11 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           for (int i = 0; i < 4; ++i) acc[hh][i] = __fmul2_rn(acc[hh][i], c2);
           if (sizeof(KV_T) == 2) {                      // O^T fragment columns are heads 2 t4 and 2 t4 + 1
             const int t4 = lane & 3;
-            if (hh == 2 * t4) { oc[0] *= corr; oc[2] *= corr; }
-            if (hh == 2 * t4 + 1) { oc[1] *= corr; oc[3] *= corr; }
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+              if (hh == 2 * t4) { oc[a][0] *= corr; oc[a][2] *= corr; }
+              if (hh == 2 * t4 + 1) { oc[a][1] *= corr; oc[a][3] *= corr; }
+            }
           }
         }
         // p for every (head, row) of the chunk's tiles (zero past the last row). bf16 rows: each pair of rows is
@@ -375,8 +381,8 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
             f0 = *reinterpret_cast<const uint2*>(ph);
             f1 = *reinterpret_cast<const uint2*>(ph + 8);
           }
-          mma_bf16_16816(oc, a0, a1, a2, a3, f0.x, f1.x);
-          mma_bf16_16816(oc, a0, a1, a2, a3, f0.y, f1.y);
+          mma_bf16_16816(oc[2 * (kk & 1)], a0, a1, a2, a3, f0.x, f1.x);
+          mma_bf16_16816(oc[2 * (kk & 1) + 1], a0, a1, a2, a3, f0.y, f1.y);
         }
       } else {
         // CUDA cores (fp32 rows): 16 lanes per row, 8 dims per lane; the row group's rows are read first
@@ -416,7 +422,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 #pragma unroll
     for (int x = 0; x < 4; ++x) {
       const int head = 2 * t4 + (x & 1), dim = 16 * mb + g + 8 * (x >> 1);
-      if (head < HP) red[(khalf * HP + head) * kHeadDim + dim] = oc[x];
+      if (head < HP) red[(khalf * HP + head) * kHeadDim + dim] = (oc[0][x] + oc[2][x]) + (oc[1][x] + oc[3][x]);
     }
     __syncthreads();
     for (int idx = tid; idx < HP * kHeadDim; idx += kThreads) {

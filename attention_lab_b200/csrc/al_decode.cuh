@@ -183,8 +183,14 @@ __device__ __forceinline__ void fma_rows8(float2 (&acc2)[V16<IDX_T>::n / 2], con
   }
 }
 
-template <typename IDX_T, bool FULLR, typename Sink>
-__device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1, const float* s_u, Sink sink) {
+struct NoPre {
+  __device__ __forceinline__ void operator()() const {}
+};
+
+// `pre` runs once, after the first two batches of loads are in flight and before u is first read (the fused kernel
+// computes u there, so its latency hides under the loads); it must be called by every thread of the CTA.
+template <typename IDX_T, bool FULLR, typename Sink, typename Pre>
+__device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1, const float* s_u, Sink sink, Pre pre) {
   const IDX_T* zseg = reinterpret_cast<const IDX_T*>(zs.z);
   const int r = FULLR ? kMaxR : zs.r, C = zs.C;
   if (zs.vec) {
@@ -203,6 +209,7 @@ __device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1,
       load_rows8<IDX_T, FULLR>(va, zc, 0, r, C);
       load_rows8<IDX_T, FULLR>(vb, zc, 8, r, C);
     }
+    pre();
 #pragma unroll 1
     for (int round = 0; round < nrounds; ++round, gi += kThreads) {
       const bool in = gi < ngr;
@@ -236,6 +243,7 @@ __device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1,
       sink.round_end(round);
     }
   } else {
+    pre();
 #pragma unroll 1
     for (int cb = c0, round = 0; cb < c1; cb += kThreads, ++round) {
       const int c = cb + threadIdx.x;
@@ -251,10 +259,11 @@ __device__ __forceinline__ void scan_columns_impl(const ZSrc zs, int c0, int c1,
 }
 
 // r == 32 (every row real) takes a version without the row clamp.
-template <typename IDX_T, typename Sink>
-__device__ __forceinline__ void scan_columns(const ZSrc zs, int c0, int c1, const float* s_u, const Sink& sink) {
-  if (zs.r == kMaxR) scan_columns_impl<IDX_T, true>(zs, c0, c1, s_u, sink);
-  else scan_columns_impl<IDX_T, false>(zs, c0, c1, s_u, sink);
+template <typename IDX_T, typename Sink, typename Pre = NoPre>
+__device__ __forceinline__ void scan_columns(const ZSrc zs, int c0, int c1, const float* s_u, const Sink& sink,
+                                             const Pre& pre = Pre()) {
+  if (zs.r == kMaxR) scan_columns_impl<IDX_T, true>(zs, c0, c1, s_u, sink, pre);
+  else scan_columns_impl<IDX_T, false>(zs, c0, c1, s_u, sink, pre);
 }
 
 // Selection state of the fused kernel at fixed shared addresses (no registers needed to reach it): the dynamic
@@ -423,6 +432,41 @@ struct SinkScores {
   __device__ __forceinline__ void round_end(int) {}
 };
 
+// One warp: the bin of a 4096-bin histogram holding the need-th largest element counted from the top bin, the
+// number of elements above that bin, and the bin's own count.
+__device__ void warp_pivot4096(const unsigned* hist, int need, int& bin_out, int& above_out, int& count_out) {
+  const int lane = threadIdx.x & 31;
+  unsigned cum = 0;
+  bin_out = 0; above_out = 0; count_out = 0;
+  for (int top = 4095; top >= 0; top -= 128) {
+    const int lo = top - 4 * lane - 3;                       // this lane's bins lo..lo+3; lane 0 holds the highest
+    const uint4 v = *reinterpret_cast<const uint4*>(hist + lo);
+    const unsigned ls = v.x + v.y + v.z + v.w;
+    const unsigned blk = __reduce_add_sync(0xffffffffu, ls);
+    if (cum + blk >= (unsigned)need) {
+      unsigned incl = ls;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      const int L = __ffs(__ballot_sync(0xffffffffu, cum + incl >= (unsigned)need)) - 1;
+      unsigned c = cum + incl - ls;                           // elements above this lane's bins
+      int b = lo, above = 0, cnt = 0;
+      const unsigned bv[4] = {v.w, v.z, v.y, v.x};            // bins lo+3 .. lo
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (cnt == 0 && c + bv[i] >= (unsigned)need) { b = lo + 3 - i; above = (int)c; cnt = (int)bv[i]; }
+        else if (cnt == 0) c += bv[i];
+      bin_out = __shfl_sync(0xffffffffu, b, L);
+      above_out = __shfl_sync(0xffffffffu, above, L);
+      count_out = __shfl_sync(0xffffffffu, cnt, L);
+      return;
+    }
+    cum += blk;
+  }
+}
+
 // Cluster-wide pivot search over the CTAs' NB-bin histograms (complete and visible cluster-wide on entry): the bin
 // holding the need-th largest element counted from the top bin, and the number of elements in the bins above it.
 // Every CTA returns the same result. CS == 1 reads its own histogram and uses block barriers only; CS > 1 sums this
@@ -492,9 +536,10 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   __shared__ float s_pre[kWarps * 32];
   __shared__ int s_sltot[kMaxCluster];
   __shared__ int s_cgt[kMaxCluster], s_ceq[kMaxCluster], s_cflag[kMaxCluster];
-  __shared__ int s_piv[2];
+  __shared__ int s_piv[4];
   __shared__ int s_ws[kWarps];
   __shared__ int s_fpre;
+  __shared__ long long s_segoff;
   __shared__ float s_m[HP], s_l[HP];
   __shared__ float s_acc[HP * kHeadDim];
 
@@ -528,26 +573,52 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
     if (tid == 0) { g_list_count = 0u; g_list_thr = 0u; }
   }
   if (p.k_new && crank == 0) write_z_column<IDX_T>(p, b, g);
-  if (p.scan) compute_u<IDX_T>(p, b, g, s_u, s_pre);     // ends with __syncthreads()
+  // selection-independent inputs of the compaction, loaded while the scan's first loads are in flight (at once when
+  // this CTA scans nothing): the segment's first candidate row, this CTA's share of F into the attend list, and
+  // (canonical order) how many F rows precede the candidates
+  const auto load_rows = [&]() {
+    const int F = p.F;
+    const int fsh0 = (crank * F) / CS, fshare = ((crank + 1) * F) / CS - fsh0;
+    for (int i = tid; i < fshare; i += kThreads)
+      s_arow[i] = checked_row(p.fixed_rows[(size_t)seg * F + fsh0 + i], p.total_rows, p.err);
+    if (tid < 32) {
+      const long long so0 = p.off_lo[seg];
+      int fp = 0;
+      if (p.canonical)
+        for (int base = 0; base < F; base += 32) {
+          const int i = base + tid;
+          fp += __popc(__ballot_sync(0xffffffffu, i < F && p.fixed_rows[(size_t)seg * F + i] < so0));
+        }
+      if (tid == 0) { s_segoff = so0; s_fpre = fp; }
+    }
+  };
+  // u is computed inside the scan, under its first loads (compute_u ends with the __syncthreads() that also
+  // publishes the cleared histogram before any key is counted); a CTA without columns needs no u
+  const auto pre_u = [&]() {
+    load_rows();
+    compute_u<IDX_T>(p, b, g, s_u, s_pre);
+  };
+  const bool scans = p.scan && nloc > 0;
+  if (!scans) load_rows();
 
   // ---------------- scan: candidate scores -> order keys ----------------
   float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
   const ZSrc zsrc{reinterpret_cast<const IDX_T*>(p.zT) + (size_t)seg * p.r * p.C, p.r, p.C, p.zvec};
-  if (p.scan && nloc > 0) {
+  if (scans) {
     if (p.select_mode == 1) {
       if (so) {
         SinkFirst<true> sk{so, p.list_off, p.cap, p.k, kb};
-        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk, pre_u);
       } else {
         SinkFirst<false> sk{nullptr, p.list_off, p.cap, p.k, kb};
-        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+        scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk, pre_u);
       }
     } else if (s_skey) {
       SinkKeys sk{s_skey, kb, so};
-      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk, pre_u);
     } else {
       SinkScores sk{so};
-      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk);
+      scan_columns<IDX_T>(zsrc, c0, c1, s_u, sk, pre_u);
     }
   }
   CSYNC();
@@ -561,7 +632,96 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   // If some CTA's list overflowed (heavy ties), steps 2-3 rescan the index columns instead of reading the list.
   uint32_t tau = 0;
   int k_rem = 0;
-  if (p.select_mode == 1) {
+  bool selected = false;
+  if (p.select_mode == 1 && CS == 1 && g_list_count <= (unsigned)p.cap) {
+    // One CTA, list complete: one warp finds the pivot bin from the histogram; if that bin holds at most kSmall
+    // keys, one list pass marks every key above it and gathers the bin's keys, and two radix passes over the
+    // gathered keys alone find the exact k-th key.
+    constexpr int kSmall = 1024;
+    if (tid < 32) {
+      int b0, gt0, n0;
+      warp_pivot4096(s_hist, p.k, b0, gt0, n0);
+      if (tid == 0) { s_piv[0] = b0; s_piv[1] = gt0; s_piv[2] = n0; }
+    }
+    __syncthreads();
+    const int b0 = s_piv[0], gt0 = s_piv[1], n0 = s_piv[2];
+    if (n0 <= kSmall) {
+      uint32_t* skey = s_hist;                           // [kSmall] keys of bin b0, then [kSmall] their columns
+      uint32_t* scol = s_hist + kSmall;
+      unsigned* whist = s_hist + 2 * kSmall;             // [1024] digit histogram of the gathered keys
+      if (tid == 0) g_list_thr = 0u;                     // reused as the gathered keys' fill counter
+      __syncthreads();
+      const int n_list = (int)g_list_count;
+      const unsigned lt = (1u << (tid & 31)) - 1u;
+      constexpr int U = 4;                               // list entries per thread and step, loads batched
+      for (int base = 0; base < n_list; base += U * kThreads) {   // uniform trip count: warp-aggregated appends
+        uint32_t key[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const int i = base + j * kThreads + tid;
+          key[j] = i < n_list ? s_lkey[i] : 0u;
+        }
+        unsigned bal[U], tot = 0;
+#pragma unroll
+        for (int j = 0; j < U; ++j) {
+          const int i = base + j * kThreads + tid;
+          const int bin = (int)(key[j] >> 20);
+          if (i < n_list && bin > b0) {
+            const uint32_t c = s_lcol[i];
+            atomicOr(&s_gt[c >> 5], 1u << (c & 31));
+            if (s_skey) s_skey[c] = key[j];
+          }
+          bal[j] = __ballot_sync(0xffffffffu, i < n_list && bin == b0);
+          tot += __popc(bal[j]);
+        }
+        if (tot) {                                       // one shared atomic per warp and step
+          unsigned o = 0;
+          if ((tid & 31) == 0) o = atomicAdd(&g_list_thr, tot);
+          o = __shfl_sync(0xffffffffu, o, 0);
+#pragma unroll
+          for (int j = 0; j < U; ++j) {
+            if ((bal[j] >> (tid & 31)) & 1u) {
+              const unsigned slot = o + __popc(bal[j] & lt);
+              skey[slot] = key[j];
+              scol[slot] = s_lcol[base + j * kThreads + tid];
+            }
+            o += __popc(bal[j]);
+          }
+        }
+      }
+      __syncthreads();
+      // two 10-bit refinement passes over the gathered keys only (block histogram + block pivot search)
+      uint32_t prefix = (uint32_t)b0 << 20, pmask = 0xfff00000u;
+      int need = p.k - gt0;
+#pragma unroll 1
+      for (int pass = 0; pass < 2; ++pass) {
+        const int shift = pass == 0 ? 10 : 0;
+        for (int i = tid; i < 1024; i += kThreads) whist[i] = 0u;
+        __syncthreads();
+        for (int i = tid; i < n0; i += kThreads) {
+          const uint32_t key = skey[i];
+          if ((key & pmask) == prefix) atomicAdd(&whist[(key >> shift) & 1023u], 1u);
+        }
+        __syncthreads();
+        int bn, above;
+        pivot_round(cluster, 1, 0, whist, nullptr, s_sltot, s_piv, s_ws, 1024, need, bn, above);
+        prefix |= (uint32_t)bn << shift;
+        pmask |= 1023u << shift;
+        need -= above;
+      }
+      for (int i = tid; i < n0; i += kThreads) {
+        const uint32_t key = skey[i], c = scol[i];
+        if (key > prefix) atomicOr(&s_gt[c >> 5], 1u << (c & 31));
+        else if (key == prefix) atomicOr(&s_eq[c >> 5], 1u << (c & 31));
+        if (s_skey && key >= prefix) s_skey[c] = key;
+      }
+      __syncthreads();
+      tau = prefix;
+      k_rem = need;
+      selected = true;
+    }
+  }
+  if (p.select_mode == 1 && !selected) {
     int b0, gt0;
     pivot_round(cluster, CS, crank, s_hist, s_slice, s_sltot, s_piv, s_ws, 4096, p.k, b0, gt0);
     const unsigned cnt = g_list_count;
@@ -614,16 +774,9 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   }
 
   // ---------------- ordered selection: chosen candidates in ascending position order ----------------
-  const long long seg_off = p.off_lo[seg];
+  const long long seg_off = s_segoff;
   const int F = p.F;
-  const int fsh0 = (crank * F) / CS, fsh1 = ((crank + 1) * F) / CS, fshare = fsh1 - fsh0;
-  if (tid == 0) {
-    int fp = 0;
-    if (p.canonical)
-      for (int i = 0; i < F; ++i) fp += (p.fixed_rows[(size_t)seg * F + i] < seg_off) ? 1 : 0;
-    s_fpre = fp;
-  }
-  __syncthreads();
+  const int fsh0 = (crank * F) / CS, fshare = ((crank + 1) * F) / CS - fsh0;
   const int out_base = p.canonical ? s_fpre : F;
   long long* ro = p.rows_out ? p.rows_out + (size_t)seg * p.S + out_base : nullptr;
   int n_sel = 0;
@@ -687,8 +840,6 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   }
   if (p.keys_out && crank == 0)
     for (int i = p.k + tid; i < p.kst; i += kThreads) p.keys_out[(size_t)seg * p.kst + i] = 0ull;   // below every key
-  for (int i = tid; i < fshare; i += kThreads)
-    s_arow[i] = checked_row(p.fixed_rows[(size_t)seg * F + fsh0 + i], p.total_rows, p.err);
   __syncthreads();
   if (p.rows_out && crank == 0 && tid < 32) {
     // F into the row list: first (reference order), or around the candidates when canonical
