@@ -31,6 +31,9 @@ struct AttendCfg {
   static constexpr int LG = kThreads / 16;                // V sweep: 16-lane row groups per CTA
   static constexpr int RPG = TR / LG;                     // V sweep: rows per row group per tile
   static constexpr int CHUNK = 512;                       // rows scored before their V sweep
+  // per-head stride of the chunk scores: CHUNK + 8 floats (= 8 mod 32 banks), so the V tile's probability fragments
+  // (8 heads x 4 lanes of 8 bytes) and the K tile's score writes spread over the banks instead of sharing one
+  static constexpr int SCS = CHUNK + 8;
   static constexpr int STAGE_BYTES = TR * ROWB;
   static constexpr int RED_BYTES = kWarps * HP * kHeadDim * 4;
   static_assert(RED_BYTES <= MIN_STAGES * STAGE_BYTES, "warp reduction buffer aliases the stage buffers");
@@ -40,7 +43,7 @@ struct AttendCfg {
   // shared memory of the engine with `stages` stages: stage buffers | chunk scores (then p) | warp maxima and sums |
   // fp32 rows only: K partial sums, q. (bf16 rows keep q in registers; it is staged in the last stage buffer.)
   static constexpr bool F32 = sizeof(KV_T) == 4;
-  static constexpr int TAIL = CHUNK * HP * 4 + 2 * kWarps * HP * 4 + (F32 ? KPARTS * TR * HP * 4 + HP * kHeadDim * 4 : 0);
+  static constexpr int TAIL = SCS * HP * 4 + 2 * kWarps * HP * 4 + (F32 ? KPARTS * TR * HP * 4 + HP * kHeadDim * 4 : 0);
   static constexpr __host__ __device__ int smem(int stages) { return stages * STAGE_BYTES + TAIL; }
   static constexpr int SMEM = MIN_STAGES * STAGE_BYTES + TAIL;
   // a staged row holds its 16-byte chunks XOR-swizzled by the row index, so both sweeps read without bank conflicts
@@ -118,7 +121,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
   const int krow = tid % Cfg::TR, kpart = tid / Cfg::TR; // K sweep row and dim part
   unsigned char* stages = dsm;
   float* s_sc = reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES);
-  float* s_wm = s_sc + Cfg::CHUNK * HP;                  // [kWarps][HP] warp maxima
+  float* s_wm = s_sc + Cfg::SCS * HP;                    // [kWarps][HP] warp maxima
   float* s_wl = s_wm + kWarps * HP;                      // [kWarps][HP] warp sums of p
   float* s_kp = s_wl + kWarps * HP;                      // fp32 rows: [KPARTS][TR][HP] partial dot products
   const unsigned char* Kb = reinterpret_cast<const unsigned char*>(Kf);
@@ -227,7 +230,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
                 const int head = 2 * t4 + j;
                 if (head < HP) {
                   const float sc = live ? c[2 * half + j] * scale_log2 : -INFINITY;
-                  s_sc[head * Cfg::CHUNK + row] = sc;
+                  s_sc[head * Cfg::SCS + row] = sc;
                   mh2[j] = fmaxf(mh2[j], sc);
                 }
               }
@@ -270,7 +273,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
 #pragma unroll
             for (int pp = 0; pp < Cfg::KPARTS; ++pp) sc += s_kp[pp * Cfg::TR * HP + i];
             sc = rs.get(row) == 0xffffffffu ? -INFINITY : sc * scale_log2;
-            s_sc[head * Cfg::CHUNK + row] = sc;
+            s_sc[head * Cfg::SCS + row] = sc;
 #pragma unroll
             for (int hh = 0; hh < HP; ++hh) mh[hh] = (hh == head) ? fmaxf(mh[hh], sc) : mh[hh];
           }
@@ -324,7 +327,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
         for (int hh = 0; hh < HP; ++hh) {
           psum[hh] = 0.f;
           const float mv = m_run[hh];
-          float* sh = s_sc + hh * Cfg::CHUNK;
+          float* sh = s_sc + hh * Cfg::SCS;
           for (int rp = tid; rp < nr / 2; rp += kThreads) {
             const float2 sv = *reinterpret_cast<const float2*>(sh + 2 * rp);
             const float p0 = (2 * rp < n && mv != -INFINITY && sv.x != -INFINITY) ? exp2f(sv.x - mv) : 0.f;
@@ -377,7 +380,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           // B fragment of head g (zero beyond HP): rows r16 + 2 t4 (+1) and + 8 (+9), packed by the p pass
           uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
           if (g < HP) {
-            const float* ph = s_sc + g * Cfg::CHUNK + t * Cfg::TR + r16 + 2 * t4;
+            const float* ph = s_sc + g * Cfg::SCS + t * Cfg::TR + r16 + 2 * t4;
             f0 = *reinterpret_cast<const uint2*>(ph);
             f1 = *reinterpret_cast<const uint2*>(ph + 8);
           }
@@ -395,7 +398,7 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           const bool ok = row < n && rs.get(row) != 0xffffffffu;
           const int rrow = ok ? row : 0;
 #pragma unroll
-          for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[hh * Cfg::CHUNK + rrow] : 0.f;
+          for (int hh = 0; hh < HP; ++hh) pr[i][hh] = ok ? s_sc[hh * Cfg::SCS + rrow] : 0.f;
           load_row2<KV_T, Cfg>(buf, rr, li, vf[i]);
         }
 #pragma unroll
@@ -511,7 +514,7 @@ template <typename KV_T, int HP>
 __device__ __forceinline__ float* stage_q(unsigned char* dsm, int nstage, const KV_T* __restrict__ qb, long long sh,
                                           int h) {
   using Cfg = AttendCfg<KV_T, HP>;
-  float* s_q = Cfg::F32 ? reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::CHUNK * HP + 2 * kWarps * HP +
+  float* s_q = Cfg::F32 ? reinterpret_cast<float*>(dsm + nstage * Cfg::STAGE_BYTES) + Cfg::SCS * HP + 2 * kWarps * HP +
                               Cfg::KPARTS * Cfg::TR * HP
                         : reinterpret_cast<float*>(dsm + (nstage - 1) * Cfg::STAGE_BYTES);
   for (int i = threadIdx.x; i < HP * kHeadDim; i += kThreads) {

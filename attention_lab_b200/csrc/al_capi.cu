@@ -144,9 +144,13 @@ constexpr int kFusedStaticBytes = 8 * 1024;
 constexpr int kAttendStaticBytes = 4 * 1024;
 
 // Attend pipeline depth (32 KB stages). Three stages keep a CTA of the fused or the attend kernel within half of an
-// SM's shared memory, so two 256-thread CTAs share each SM and one's selection or attend overlaps the other's scan.
+// SM's shared memory, so two 256-thread CTAs share each SM (measured: six 16 KB stages of 64-row tiles ran slower,
+// the engine is bound by its per-tile work rather than by the bytes in flight).
 constexpr int kStages = 3;
 constexpr int kFusedStages = 3;
+// Dynamic shared memory of one CTA when two share an SM: half of the SM's 228 KB, less the 1 KB the runtime reserves
+// per CTA and a 4 KB allowance for the kernels' static shared memory.
+constexpr long long kHalfSmBudget = 228 * 1024 / 2 - 1024 - 4096;
 
 int engine_smem(int kv_dtype, int hp, int stages = kStages) {
   switch (kv_dtype * 8 + hp) {
@@ -267,7 +271,9 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
       cap_min = std::min(p.cpc, round_cols + 6 * p.k + 1024);
     }
     const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
+    // the deepest pipeline that leaves room for two CTAs per SM, else the deepest that fits at all
     bool fits = false;
+    for (int pass = 0; pass < 2 && !fits; ++pass)
     for (int st = kFusedStages; st >= 3 && !fits; --st) {
       const size_t eng = attend ? (size_t)engine_smem(kv_dtype, hp, st) : 0;
       p.cap = 0;
@@ -283,7 +289,7 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
       p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
       smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
       p.nstage = st;
-      fits = (long long)smem <= budget;
+      fits = (long long)smem <= (pass == 0 ? kHalfSmBudget : budget);
     }
     if (fits) break;
     if (cluster > 0 || cs >= kMaxCluster)
@@ -382,10 +388,16 @@ static int run_attend(AttendParams p, int kv_dtype, int d, int n_all, int cluste
   }
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
   p.rows_cap = p.mode == 0 ? std::max(1, (n_all + cs - 1) / cs) : 0;
-  p.nstage = kStages;
-  const size_t smem = (size_t)engine_smem(kv_dtype, hp) + (size_t)p.rows_cap * 4;
-  if ((long long)smem > di->max_smem_optin - kAttendStaticBytes)
-    return fail(AL_EUNSUPPORTED, "row list too long for cluster %d (%zu bytes of shared memory)", cs, smem);
+  // the deepest pipeline that leaves room for two CTAs per SM, else the deepest that fits at all
+  size_t smem = 0;
+  bool fits = false;
+  for (int pass = 0; pass < 2 && !fits; ++pass)
+    for (int st = kStages; st >= 3 && !fits; --st) {
+      smem = (size_t)engine_smem(kv_dtype, hp, st) + (size_t)p.rows_cap * 4;
+      p.nstage = st;
+      fits = (long long)smem <= (pass == 0 ? kHalfSmBudget : (long long)(di->max_smem_optin - kAttendStaticBytes));
+    }
+  if (!fits) return fail(AL_EUNSUPPORTED, "row list too long for cluster %d (%zu bytes of shared memory)", cs, smem);
   p.err = di->err;
   dim3 grid((unsigned)cs, (unsigned)(p.B * p.G), 1);
   return dispatch_attend(p, kv_dtype, hp, grid, cs, smem, stream);
