@@ -66,13 +66,19 @@ __device__ __forceinline__ void issue_tile(const unsigned char* __restrict__ cac
   constexpr int RSTEP = kThreads / Cfg::NCH;              // rows between a thread's chunks
   const int ch = threadIdx.x % Cfg::NCH, r0 = threadIdx.x / Cfg::NCH;
   const unsigned char* src = cache + ch * 16;
+  // all row ids first (their shared-memory loads overlap), then the copies: a copy's memory clobber would otherwise
+  // hold each next id load behind it
+  uint32_t id[CPT];
+#pragma unroll
+  for (int j = 0; j < CPT; ++j) {
+    const int row = row0 + r0 + j * RSTEP;
+    id[j] = row < n ? rows.get(row) : 0xffffffffu;
+  }
 #pragma unroll
   for (int j = 0; j < CPT; ++j) {
     const int rr = r0 + j * RSTEP;
-    const int row = row0 + rr;
-    const uint32_t id = row < n ? rows.get(row) : 0xffffffffu;
     unsigned char* dst = buf + rr * Cfg::ROWB + Cfg::swz(rr, ch) * 16;
-    if (id != 0xffffffffu) cp_async16(dst, src + (size_t)id * Cfg::ROWB);
+    if (id[j] != 0xffffffffu) cp_async16(dst, src + (size_t)id[j] * Cfg::ROWB);
     else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);   // rows not read hold zeros
   }
 }
@@ -211,12 +217,13 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
           const int lr = 16 * w + (lane & 15), lhi = lane >> 4;
           const uint32_t rowaddr = smem_addr(buf + lr * Cfg::ROWB);
           float ce[4] = {0.f, 0.f, 0.f, 0.f}, co[4] = {0.f, 0.f, 0.f, 0.f};   // even / odd dim steps
+          uint32_t a[8][4];                               // every fragment first, then the MMAs
 #pragma unroll
-          for (int ks = 0; ks < 8; ++ks) {
-            uint32_t a0, a1, a2, a3;
-            ldmatrix_x4(rowaddr + (uint32_t)(Cfg::swz(lr, 2 * ks + lhi) << 4), a0, a1, a2, a3);
-            mma_bf16_16816((ks & 1) ? co : ce, a0, a1, a2, a3, qb[ks][0], qb[ks][1]);
-          }
+          for (int ks = 0; ks < 8; ++ks)
+            ldmatrix_x4(rowaddr + (uint32_t)(Cfg::swz(lr, 2 * ks + lhi) << 4), a[ks][0], a[ks][1], a[ks][2], a[ks][3]);
+#pragma unroll
+          for (int ks = 0; ks < 8; ++ks)
+            mma_bf16_16816((ks & 1) ? co : ce, a[ks][0], a[ks][1], a[ks][2], a[ks][3], qb[ks][0], qb[ks][1]);
           const float c[4] = {ce[0] + co[0], ce[1] + co[1], ce[2] + co[2], ce[3] + co[3]};
           // c0, c1: row 16w + g, heads 2 t4, 2 t4 + 1; c2, c3: row 16w + g + 8
           const int g = lane >> 2, t4 = lane & 3;
@@ -371,21 +378,28 @@ __device__ void attend_rows(const KV_T* __restrict__ Kf, const KV_T* __restrict_
         const int mb = w & 7, khalf = w >> 3;
         const int g = lane >> 2, t4 = lane & 3;
         const int vr_lane = (lane & 7) + ((lane >> 4) << 3), vc_lane = 2 * mb + ((lane >> 3) & 1);
+        constexpr int NK = RPW / 16;                      // row steps of 16
+        uint32_t a[NK][4];                                // every fragment of the tile first, then the MMAs
+        uint2 f0[NK], f1[NK];
 #pragma unroll
-        for (int kk = 0; kk < RPW / 16; ++kk) {
+        for (int kk = 0; kk < NK; ++kk) {
           const int r16 = RPW * khalf + 16 * kk;          // first row of this step within the tile
           const int vr = r16 + vr_lane;
-          uint32_t a0, a1, a2, a3;
-          ldmatrix_x4_trans(smem_addr(buf + vr * Cfg::ROWB + Cfg::swz(vr, vc_lane) * 16), a0, a1, a2, a3);
+          ldmatrix_x4_trans(smem_addr(buf + vr * Cfg::ROWB + Cfg::swz(vr, vc_lane) * 16), a[kk][0], a[kk][1], a[kk][2],
+                            a[kk][3]);
           // B fragment of head g (zero beyond HP): rows r16 + 2 t4 (+1) and + 8 (+9), packed by the p pass
-          uint2 f0 = make_uint2(0u, 0u), f1 = make_uint2(0u, 0u);
+          f0[kk] = make_uint2(0u, 0u);
+          f1[kk] = make_uint2(0u, 0u);
           if (g < HP) {
             const float* ph = s_sc + g * Cfg::SCS + t * Cfg::TR + r16 + 2 * t4;
-            f0 = *reinterpret_cast<const uint2*>(ph);
-            f1 = *reinterpret_cast<const uint2*>(ph + 8);
+            f0[kk] = *reinterpret_cast<const uint2*>(ph);
+            f1[kk] = *reinterpret_cast<const uint2*>(ph + 8);
           }
-          mma_bf16_16816(oc[2 * (kk & 1)], a0, a1, a2, a3, f0.x, f1.x);
-          mma_bf16_16816(oc[2 * (kk & 1) + 1], a0, a1, a2, a3, f0.y, f1.y);
+        }
+#pragma unroll
+        for (int kk = 0; kk < NK; ++kk) {
+          mma_bf16_16816(oc[2 * (kk & 1)], a[kk][0], a[kk][1], a[kk][2], a[kk][3], f0[kk].x, f1[kk].x);
+          mma_bf16_16816(oc[2 * (kk & 1) + 1], a[kk][0], a[kk][1], a[kk][2], a[kk][3], f0[kk].y, f1[kk].y);
         }
       } else {
         // CUDA cores (fp32 rows): 16 lanes per row, 8 dims per lane; the row group's rows are read first
