@@ -288,29 +288,50 @@ __device__ void raise_threshold(const unsigned* hist, unsigned* thr, int k) {
   if (lane == 0) t0 = (int)*reinterpret_cast<volatile unsigned*>(thr);
   t0 = __shfl_sync(0xffffffffu, t0, 0);
   unsigned cum = 0;
-  for (int top = 4095; top >= t0; top -= 128) {
-    const int lo = top - 4 * lane - 3;                       // this lane's bins lo..lo+3; lane 0 holds the highest
-    const uint4 v = lds_volatile_u4(hist + lo);
-    const unsigned ls = v.x + v.y + v.z + v.w;
-    const unsigned blk = __reduce_add_sync(0xffffffffu, ls);
-    if (cum + blk >= (unsigned)k) {
-      unsigned incl = ls;
+  // four 128-bin blocks per step, their loads and sums independent; block i of a step covers bins
+  // [top - 128 i - 127, top - 128 i], lane L holding its 4 bins top - 128 i - 4 L - 3 .. top - 128 i - 4 L
+  for (int top = 4095; top >= t0; top -= 512) {
+    uint4 v[4];
+    unsigned ls[4], blk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = lds_volatile_u4(hist + (top - 128 * i - 4 * lane - 3));
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      ls[i] = v[i].x + v[i].y + v[i].z + v[i].w;
+      blk[i] = __reduce_add_sync(0xffffffffu, ls[i]);
+    }
+    int ib = -1;                                             // the block where the count from the top reaches k
+    unsigned before = cum;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (ib < 0) {
+        if (before + blk[i] >= (unsigned)k) ib = i;
+        else before += blk[i];
+      }
+    if (ib >= 0) {
+      uint4 vv = v[0];
+      unsigned lss = ls[0];
+#pragma unroll
+      for (int i = 1; i < 4; ++i)
+        if (i == ib) { vv = v[i]; lss = ls[i]; }
+      const int lo = top - 128 * ib - 4 * lane - 3;
+      unsigned incl = lss;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const unsigned n = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += n;
       }
-      const int L = __ffs(__ballot_sync(0xffffffffu, cum + incl >= (unsigned)k)) - 1;
-      int b = lo;
-      unsigned c = cum + incl - ls;
-      if ((c += v.w) >= (unsigned)k) b = lo + 3;
-      else if ((c += v.z) >= (unsigned)k) b = lo + 2;
-      else if ((c += v.y) >= (unsigned)k) b = lo + 1;
-      b = __shfl_sync(0xffffffffu, b, L);
-      if (lane == 0 && b > t0) *reinterpret_cast<volatile unsigned*>(thr) = (unsigned)b;
+      const int L = __ffs(__ballot_sync(0xffffffffu, before + incl >= (unsigned)k)) - 1;
+      int bn = lo;
+      unsigned c = before + incl - lss;
+      if ((c += vv.w) >= (unsigned)k) bn = lo + 3;
+      else if ((c += vv.z) >= (unsigned)k) bn = lo + 2;
+      else if ((c += vv.y) >= (unsigned)k) bn = lo + 1;
+      bn = __shfl_sync(0xffffffffu, bn, L);
+      if (lane == 0 && bn > t0) *reinterpret_cast<volatile unsigned*>(thr) = (unsigned)bn;
       return;
     }
-    cum += blk;
+    cum = before;
   }
 }
 
@@ -575,31 +596,39 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   if (p.k_new && crank == 0) write_z_column<IDX_T>(p, b, g);
   // selection-independent inputs of the compaction, loaded while the scan's first loads are in flight (at once when
   // this CTA scans nothing): the segment's first candidate row, this CTA's share of F into the attend list, and
-  // (canonical order) how many F rows precede the candidates
-  const auto load_rows = [&]() {
+  // (canonical order) how many F rows precede the candidates. With F <= kThreads (one row per thread) the loads are
+  // issued before u is computed and consumed after it, so the two latencies overlap.
+  const auto load_rows = [&](auto&& between) {
     const int F = p.F;
     const int fsh0 = (crank * F) / CS, fshare = ((crank + 1) * F) / CS - fsh0;
-    for (int i = tid; i < fshare; i += kThreads)
-      s_arow[i] = checked_row(p.fixed_rows[(size_t)seg * F + fsh0 + i], p.total_rows, p.err);
-    if (tid < 32) {
+    if (F <= kThreads) {
+      const long long fr = tid < F ? p.fixed_rows[(size_t)seg * F + tid] : 0;
       const long long so0 = p.off_lo[seg];
-      int fp = 0;
-      if (p.canonical)
-        for (int base = 0; base < F; base += 32) {
-          const int i = base + tid;
-          fp += __popc(__ballot_sync(0xffffffffu, i < F && p.fixed_rows[(size_t)seg * F + i] < so0));
-        }
+      between();
+      if (tid >= fsh0 && tid < fsh0 + fshare) s_arow[tid - fsh0] = checked_row(fr, p.total_rows, p.err);
+      const int fp = __syncthreads_count(p.canonical && tid < F && fr < so0);
       if (tid == 0) { s_segoff = so0; s_fpre = fp; }
+    } else {
+      between();
+      for (int i = tid; i < fshare; i += kThreads)
+        s_arow[i] = checked_row(p.fixed_rows[(size_t)seg * F + fsh0 + i], p.total_rows, p.err);
+      if (tid < 32) {
+        const long long so0 = p.off_lo[seg];
+        int fp = 0;
+        if (p.canonical)
+          for (int base = 0; base < F; base += 32) {
+            const int i = base + tid;
+            fp += __popc(__ballot_sync(0xffffffffu, i < F && p.fixed_rows[(size_t)seg * F + i] < so0));
+          }
+        if (tid == 0) { s_segoff = so0; s_fpre = fp; }
+      }
     }
   };
   // u is computed inside the scan, under its first loads (compute_u ends with the __syncthreads() that also
   // publishes the cleared histogram before any key is counted); a CTA without columns needs no u
-  const auto pre_u = [&]() {
-    load_rows();
-    compute_u<IDX_T>(p, b, g, s_u, s_pre);
-  };
+  const auto pre_u = [&]() { load_rows([&]() { compute_u<IDX_T>(p, b, g, s_u, s_pre); }); };
   const bool scans = p.scan && nloc > 0;
-  if (!scans) load_rows();
+  if (!scans) load_rows([]() {});
 
   // ---------------- scan: candidate scores -> order keys ----------------
   float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
