@@ -202,6 +202,32 @@ def select_rows(u, zT, fixed_rows, off_lo, lo: int, hi: int, k: int) -> np.ndarr
     return np.concatenate([fixed_rows, top + off_lo], axis=-1).reshape(-1)
 
 
+def select_rows_recent(fixed_rows, off_lo, lo: int, hi: int, k: int) -> np.ndarray:
+    """Selector B: F, then the k most recent candidates [hi - k, hi) as flat rows: decode.py:94-107."""
+    B, G = fixed_rows.shape[:2]
+    if k <= 0:
+        return fixed_rows.reshape(-1).copy()
+    M = hi - lo
+    if k > M:
+        raise ValueError(f"k={k} exceeds the candidate count {M}")
+    rel = np.broadcast_to(np.arange(M - k, M, dtype=np.int64), (B, G, k))
+    return np.concatenate([fixed_rows, rel + off_lo], axis=-1).reshape(-1)
+
+
+def select_rows_uniform(fixed_rows, off_lo, lo: int, hi: int, k: int, *, rng) -> np.ndarray:
+    """Selector C: F, then k candidates drawn uniformly without replacement per (batch, group), as the top-k of
+    i.i.d. float64 uniforms from the numpy Generator `rng` (drawn [B,G,M] in one call): decode.py:110-127."""
+    B, G = fixed_rows.shape[:2]
+    if k <= 0:
+        return fixed_rows.reshape(-1).copy()
+    M = hi - lo
+    if k > M:
+        raise ValueError(f"k={k} exceeds the candidate count {M}")
+    u = rng.random((B, G, M), dtype=np.float64)
+    rel = topk_indices(u, k)
+    return np.concatenate([fixed_rows, rel + off_lo], axis=-1).reshape(-1)
+
+
 def subset_attention(q: np.ndarray, k_sub: np.ndarray, v_sub: np.ndarray, scale=None) -> np.ndarray:
     """softmax(q.k_sub^T * scale) @ v_sub with the h query heads sharing the subset: sparse.py:40-60.
 

@@ -209,6 +209,30 @@ def test_gathered_rows_are_original_positions_and_order_does_not_matter():
     assert np.abs(a[:, :, 0] - a[:, :, 1]).max() > 1e-2, "the heads of a group share rows, not answers"
 
 
+@pytest.mark.parametrize("selector", ["B_recent", "C_uniform"])
+def test_selectors_b_and_c_attend_through_the_gathered_kernel(selector):
+    """The reference's B and C selectors (decode.py:94-127) build their row lists on the host and attend through
+    gathered_decode_step_kernel; here that kernel is the CUDA one. Same F, same budget, the same rows as the oracle's
+    restatement of each selector, outputs within the tolerance of tests/parity.py."""
+    al, lib = _al()
+    for name in ("c1_bf16kv", "canonical"):
+        case = cs.CASES[name]
+        t = cs.build(case)
+        c = cs.step_constants(case)
+        g = gpu(t)
+        n = cs.to_np
+        if selector == "B_recent":
+            rows = orc.select_rows_recent(c["fixed_rows"], c["off_lo"], c["lo"], c["hi"], c["k"])
+        else:
+            rows = orc.select_rows_uniform(c["fixed_rows"], c["off_lo"], c["lo"], c["hi"], c["k"],
+                                           rng=np.random.default_rng(1234))
+        want = orc.gathered_decode_step(n(t["q"]), n(t["k"]), n(t["v"]), rows, c["S"], 1 / math.sqrt(case.d))
+        out = al.gathered_decode_step_kernel(g["q"], g["k"], g["v"], torch.from_numpy(rows).to(DEV), c["S"],
+                                             scale=1 / math.sqrt(case.d))
+        check_out(out.float().cpu().numpy(), want, case.kv_dtype, f"{selector} {name}")
+    assert lib.device_status() == 0
+
+
 def test_select_rows_and_indexer_ops_match_the_oracle():
     al, lib = _al()
     case, gd = cs.CASES["batch2_h4"], golden("batch2_h4")

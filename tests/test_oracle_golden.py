@@ -169,3 +169,17 @@ def test_context_split_protocol_equals_single_device():
     merged = orc.lse_merge([p[0] for p in parts], [p[1] for p in parts], [p[2] for p in parts])
     full = orc.subset_attention(q[None, None, :, None, :], K[sel][None, None], V[sel][None, None], 1 / math.sqrt(d))
     assert np.abs(merged - full[0, 0, :, 0, :]).max() < 1e-12
+
+
+def test_selectors_b_and_c_known_answers():
+    """B takes the k newest candidates after F (decode.py:94-107); C draws a uniform k-subset per (batch, group) from
+    the caller's generator, so the same seed gives the same rows (decode.py:110-127)."""
+    fixed = np.array([[[0, 1, 2, 3, 90, 91]]], dtype=np.int64)
+    off_lo = np.array([[[4]]], dtype=np.int64)
+    rows = orc.select_rows_recent(fixed, off_lo, 4, 90, 5)
+    assert rows.tolist() == [0, 1, 2, 3, 90, 91, 85, 86, 87, 88, 89]
+    a = orc.select_rows_uniform(fixed, off_lo, 4, 90, 7, rng=np.random.default_rng(11))
+    b = orc.select_rows_uniform(fixed, off_lo, 4, 90, 7, rng=np.random.default_rng(11))
+    assert np.array_equal(a, b) and len(set(a[6:].tolist())) == 7 and all(4 <= r < 90 for r in a[6:])
+    with pytest.raises(ValueError):
+        orc.select_rows_recent(fixed, off_lo, 4, 90, 87)
