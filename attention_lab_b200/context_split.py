@@ -129,9 +129,10 @@ class CudaContextOps:
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
     if world == 1:
         return t.unsqueeze(0).contiguous()
-    buf = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-    dist.all_gather(list(buf.unbind(0)), t.contiguous(), group=group)
-    return buf
+    t = t.contiguous()
+    buf = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(buf, t, group=group)            # one call, ranks concatenated along dim 0
+    return buf.view((world,) + tuple(t.shape))
 
 
 def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan: ShardPlan, *,

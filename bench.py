@@ -59,6 +59,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override the workload's layer count (profiling cases)")
     ap.add_argument("--context-split", action="store_true",
                     help="C4 measurement: one sequence split over the torchrun ranks (attention_lab_b200.context_split)")
+    ap.add_argument("--no-graph", action="store_true", help="context split: launch every step from the host")
     return ap.parse_args()
 
 
@@ -252,15 +253,26 @@ def run_context_split(args):
 
     def step():
         return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=kpn)
-    for _ in range(max(3, args.warmup)):
-        step()
+    side = torch.cuda.Stream(device=dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(max(3, args.warmup)):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = None
+    if not args.no_graph:          # the whole protocol (kernels and both all-gathers) as one CUDA graph
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+    run = graph.replay if graph is not None else step
+    run()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        step()
+        run()
     e1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -277,10 +289,11 @@ def run_context_split(args):
                           "warmup": max(3, args.warmup), "higher_is_better": False, "scaling": "strong",
                           "dtype": "bf16", "data": "synthetic",
                           "config": {"workload": desc + f", split over {world} rank(s)", "k": lg["k"], "S": lg["S"],
-                                     "shard_capacity": cs_},
+                                     "shard_capacity": cs_, "cuda_graph": graph is not None},
                           "ledger_bytes": lg["d_s1_per_layer_request"],
                           "achieved_gbs_aggregate": round(lg["d_s1_per_layer_request"] / (ms * 1e-3) / 1e9, 1),
                           "peak_gbs_per_gpu": peak}))
+    del graph, run                 # a graph holding NCCL work is released before the process group
     if world > 1:
         dist.destroy_process_group()
 
