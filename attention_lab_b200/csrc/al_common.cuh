@@ -16,8 +16,6 @@ constexpr int kMaxCluster = 16;            // CTAs per (batch, group) segment
 
 // Error bits OR-ed into g_al_error by kernels (read and cleared by al_device_status()).
 constexpr unsigned kErrRowRange = 1u;      // a row id outside [0, B*G*C) was skipped
-constexpr unsigned kErrCluster = 2u;       // launch shape did not match the cluster the kernel expects
-constexpr unsigned kErrTimeout = 4u;       // a bounded wait on a bulk-copy barrier gave up
 
 // ------------------------------------------------------------------------------------------------ conversions
 template <typename T> __device__ __forceinline__ float tof(T x);
@@ -83,52 +81,8 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
   }
 }
 
-// Exclusive prefix sum of one int per lane within a warp; *total receives the warp total.
-__device__ __forceinline__ int warp_exclusive_scan(int v, int* total) {
-  const int lane = threadIdx.x & 31;
-  int x = v;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, x, o);
-    if (lane >= o) x += n;
-  }
-  *total = __shfl_sync(0xffffffffu, x, 31);
-  return x - v;
-}
-
-// ------------------------------------------------------------------------------------------------ bulk copies
-// One-dimensional bulk copies global -> shared (the TMA engine, no tensor map, no multicast), completed on an
-// mbarrier through its transaction count.
+// Shared-memory address of a generic pointer into shared memory (for ldmatrix and inline-PTX shared accesses).
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}\n"
-               ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  uint32_t ok;
-  asm volatile("{\n .reg .pred P;\n mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n selp.u32 %0, 1, 0, P;\n}\n"
-               : "=r"(ok) : "r"(smem_addr(bar)), "r"(parity) : "memory");
-  return ok != 0;
-}
-// Wait for the phase of `parity` to complete. Bounded: after 2^22 tries (each may suspend the thread briefly) the
-// error bit is set and a second bounded wait lets copies still in flight land before the caller moves on.
-__device__ __forceinline__ void mbar_wait(uint64_t* bar, unsigned parity, unsigned* err) {
-  for (int i = 0; i < (1 << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return;
-  atomicOr(err, kErrTimeout);
-  for (int i = 0; i < (1 << 22); ++i)
-    if (mbar_try_wait(bar, parity)) return;
-}
 
 // ------------------------------------------------------------------------------------------------ tensor cores
 // ldmatrix x4: four 8x8 bf16 matrices whose row addresses lanes 0-7, 8-15, 16-23, 24-31 supply.

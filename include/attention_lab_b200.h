@@ -38,7 +38,7 @@ const char* al_last_error(void);
 int al_version(void);
 
 /* Synchronises the current device, then returns (and clears) the error bits kernels raised since the last call:
- * 1 = a row id outside [0, B*G*C) was skipped, 2 = a launch had an unexpected cluster shape. */
+ * 1 = a row id outside [0, B*G*C) was skipped (the row is not read). */
 int al_device_status(unsigned* error_bits);
 
 /* a8: one layer's sparse decode step, fused into one launch (replaces attention-lab
