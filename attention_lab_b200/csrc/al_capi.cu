@@ -9,6 +9,7 @@
 
 #include "al_context.cuh"
 #include "al_index.cuh"
+#include "al_prefill.cuh"
 #include "../../include/attention_lab_b200.h"
 
 namespace al {
@@ -612,6 +613,33 @@ int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void
   if (out_dtype == AL_BF16) lse_merge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<__nv_bfloat16*>(out));
   else lse_merge_kernel<float><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<float*>(out));
   return plain_launch_check("lse_merge_kernel");
+}
+
+int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,
+                          int H, int T, int C, int r, int q_pos0, int k, int kcap, int* idx_out, float* scores_out,
+                          void* stream) {
+  if (!u || !zT || !idx_out) return fail(AL_EINVAL, "null pointer argument");
+  if (r != kPfR) return fail(AL_EUNSUPPORTED, "index dimension r must be %d, got %d", kPfR, r);
+  if (H <= 0 || T <= 0 || C <= 0) return fail(AL_EINVAL, "H, T and C must be positive");
+  if (H > 65535) return fail(AL_EUNSUPPORTED, "at most 65535 heads");
+  if (q_pos0 < 0) return fail(AL_EINVAL, "negative first query position");
+  if ((long long)q_pos0 + T > C) return fail(AL_EINVAL, "query positions [%d, %lld) exceed the table's %d columns", q_pos0,
+                                             (long long)q_pos0 + T, C);
+  if ((long long)q_pos0 + T > 65536) return fail(AL_EUNSUPPORTED, "legal lengths above 65536 are not supported");
+  if (k < 0 || kcap < k) return fail(AL_EINVAL, "need 0 <= k <= kcap (k=%d, kcap=%d)", k, kcap);
+  if (C % 8 || z_ld % 8 || z_sh % 8 || (reinterpret_cast<uintptr_t>(zT) & 15))
+    return fail(AL_EUNSUPPORTED, "zT needs 16-byte aligned rows (C, row and head strides multiples of 8)");
+  if (z_ld < C || u_st < kPfR) return fail(AL_EINVAL, "strides smaller than the rows they step over");
+  if (u_st % 2 || u_sh % 2 || (reinterpret_cast<uintptr_t>(u) & 3)) return fail(AL_EUNSUPPORTED, "u needs 4-byte aligned rows");
+  int rc = prepare_kernel(prefill_topk_kernel, kPfSmem, 1);
+  if (rc) return rc;
+  PrefillParams p{};
+  p.u = static_cast<const __nv_bfloat16*>(u); p.u_sh = u_sh; p.u_st = u_st;
+  p.zT = static_cast<const __nv_bfloat16*>(zT); p.z_sh = z_sh; p.z_ld = z_ld;
+  p.T = T; p.C = C; p.q_pos0 = q_pos0; p.k = k; p.kcap = kcap; p.idx = idx_out; p.scores = scores_out;
+  const dim3 grid((unsigned)((T + kPfRows - 1) / kPfRows), (unsigned)H);
+  prefill_topk_kernel<<<grid, kThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(p);
+  return plain_launch_check("prefill_topk_kernel");
 }
 
 }  // extern "C"

@@ -416,3 +416,33 @@ def lse_merge(all_parts, dtype=torch.bfloat16):
     with torch.cuda.device(dev):
         _lib.check(lib.al_lse_merge(all_parts.data_ptr(), world, B, G, h, d2 - 2, out.data_ptr(), code, _stream(dev)))
     return out
+
+
+def prefill_score_topk(u: torch.Tensor, zT: torch.Tensor, k: int = 256, *, q_pos0: int = 0, kcap=None,
+                       scores_out=None) -> torch.Tensor:
+    """Batched prefill scorer (config C5): for every query row t of a prefill chunk (position q_pos0 + t) and every
+    KV head, the top min(k, M) candidates of a decode step at legal length q_pos0 + t + 1 (selection.py:71-79,
+    decode.py:86-93, ties to the smaller position) under the scores u[h, t] . zT[h, :, c].
+
+    u [H,T,r] bf16 and zT [H,r,C] bf16 (last dims contiguous; r = 32). Returns int32 [H,T,kcap] (kcap defaults to
+    k): the chosen positions in ascending order, then -1. `scores_out` (fp32 [H,T,C], contiguous) receives the
+    scores of the candidate columns, for diagnostics."""
+    dev = _cuda(u, zT, scores_out)
+    if u.dim() != 3 or zT.dim() != 3 or u.dtype != torch.bfloat16 or zT.dtype != torch.bfloat16:
+        raise ValueError("u must be bf16 [H,T,r] and zT bf16 [H,r,C]")
+    if u.stride(2) != 1 or zT.stride(2) != 1:
+        raise ValueError("u and zT need a contiguous last dimension")
+    H, T, r = u.shape
+    if zT.shape[0] != H or zT.shape[1] != r:
+        raise ValueError(f"zT {tuple(zT.shape)} does not match u {tuple(u.shape)}")
+    C = zT.shape[2]
+    kcap = int(k) if kcap is None else int(kcap)
+    if scores_out is not None and (scores_out.shape != (H, T, C) or scores_out.dtype != torch.float32
+                                   or not scores_out.is_contiguous()):
+        raise ValueError("scores_out must be a contiguous float32 [H,T,C] tensor")
+    out = torch.empty((H, T, kcap), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_prefill_score_topk(u.data_ptr(), u.stride(0), u.stride(1), zT.data_ptr(), zT.stride(0),
+                                                     zT.stride(1), H, T, C, r, int(q_pos0), int(k), kcap,
+                                                     out.data_ptr(), _ptr(scores_out), _stream(dev)))
+    return out

@@ -202,6 +202,29 @@ def select_rows(u, zT, fixed_rows, off_lo, lo: int, hi: int, k: int) -> np.ndarr
     return np.concatenate([fixed_rows, top + off_lo], axis=-1).reshape(-1)
 
 
+def prefill_topk(u: np.ndarray, zT: np.ndarray, q_pos0: int, k: int, kcap=None, scores=None) -> np.ndarray:
+    """Batched prefill scorer (config C5): for every query row t (position q_pos0 + t) of every head, the candidates
+    of a decode step at legal length q_pos0 + t + 1 (selection.py:71-79) ranked by decode.py:86-93's single top-k
+    (ties to the smaller position, topk_indices above), chosen positions in ascending order then -1 up to kcap.
+
+    u [H,T,r], zT [H,r,C]. Scores are float64 u.zT unless `scores` ([H,T,C], e.g. a kernel's own fp32 scores) is
+    given, in which case the selection is restated on exactly those values."""
+    H, T, _ = u.shape
+    kcap = int(k) if kcap is None else int(kcap)
+    out = np.full((H, T, kcap), -1, dtype=np.int32)
+    for t in range(T):
+        lay = selection_layout(q_pos0 + t + 1)
+        kk = lay.clamp_k(k)
+        if kk == 0:
+            continue
+        if scores is None:
+            s = np.einsum("hj,hjc->hc", u[:, t].astype(np.float64), zT[:, :, lay.lo:lay.hi].astype(np.float64))
+        else:
+            s = np.asarray(scores[:, t, lay.lo:lay.hi], dtype=np.float64)
+        out[:, t, :kk] = np.sort(topk_indices(s, kk) + lay.lo, axis=-1)
+    return out
+
+
 def select_rows_recent(fixed_rows, off_lo, lo: int, hi: int, k: int) -> np.ndarray:
     """Selector B: F, then the k most recent candidates [hi - k, hi) as flat rows: decode.py:94-107."""
     B, G = fixed_rows.shape[:2]
