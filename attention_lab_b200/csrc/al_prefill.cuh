@@ -26,7 +26,9 @@ constexpr int kPfR = 32;             // index dimension r
 constexpr int kPfRowPad = kPfCols + 8;   // padded tile row (bf16): ldmatrix rows land in distinct banks
 constexpr int kPfBins = 2048;        // 11-bit digits; packed two 16-bit counters per word
 constexpr int kPfHistWords = kPfRows * kPfBins / 2;
-constexpr size_t kPfSmem = (size_t)kPfHistWords * 4 + 2 * (size_t)kPfR * kPfRowPad * 2 + 2 * kPfRows * 4 * 4;
+constexpr int kPfStages = 4;         // zT tiles in flight: three ahead of the one being scored
+constexpr size_t kPfTileBytes = (size_t)kPfR * kPfRowPad * 2;
+constexpr size_t kPfSmem = (size_t)kPfHistWords * 4 + kPfStages * kPfTileBytes + 2 * kPfRows * 4 * 4;
 
 struct PrefillParams {
   const __nv_bfloat16* u;      // [H, T, 32]
@@ -84,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_topk_kernel(PrefillParams
   extern __shared__ __align__(128) unsigned char pf_smem[];
   uint32_t* hist = reinterpret_cast<uint32_t*>(pf_smem);
   __nv_bfloat16* tiles = reinterpret_cast<__nv_bfloat16*>(pf_smem + (size_t)kPfHistWords * 4);
-  uint32_t* m_gt = reinterpret_cast<uint32_t*>(pf_smem + (size_t)kPfHistWords * 4 + 2 * kPfR * kPfRowPad * 2);
+  uint32_t* m_gt = reinterpret_cast<uint32_t*>(pf_smem + (size_t)kPfHistWords * 4 + kPfStages * kPfTileBytes);
   uint32_t* m_eq = m_gt + kPfRows * 4;
   __shared__ int s_lo[kPfRows], s_hi[kPfRows], s_shift[kPfRows], s_eqb[kPfRows], s_outb[kPfRows];
   __shared__ uint32_t s_pref[kPfRows], s_need[kPfRows];
@@ -174,14 +176,36 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_topk_kernel(PrefillParams
       if (!s_any && !(sweep == 0 && p.scores)) continue;
     }
     if (ntiles == 0) break;
-    load_tile(0, 0);
+    // this thread's two rows (g and g + 8), read once per sweep; tiles wholly inside every row's candidate range
+    // skip the per-key range checks
+    int lo2[2], hi2[2], st2[2], sh2[2];
+    uint32_t pf2[2];
+    bool eq2[2];
+    int lo_max = 0, hi_min = 1 << 30;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int rr = g + 8 * h;
+      lo2[h] = s_lo[rr]; hi2[h] = s_hi[rr]; st2[h] = s_state[rr]; sh2[h] = s_shift[rr];
+      pf2[h] = s_pref[rr]; eq2[h] = s_need[rr] > 0;
+    }
+#pragma unroll 1
+    for (int r = 0; r < kPfRows; ++r) { lo_max = max(lo_max, s_lo[r]); hi_min = min(hi_min, s_hi[r]); }
+    const int sh_cmp = sweep == 1 ? 21 : 10;
+#pragma unroll
+    for (int st = 0; st < kPfStages - 1; ++st) {
+      if (st < ntiles) load_tile(st, st);
+      else cp_async_commit();
+    }
 #pragma unroll 1
     for (int ti = 0; ti < ntiles; ++ti) {
-      if (ti + 1 < ntiles) { load_tile(ti + 1, (ti + 1) & 1); cp_async_wait<1>(); }
-      else cp_async_wait<0>();
+      // one group per tile, empty past the end: tile ti is complete once at most kPfStages - 1 groups are pending
+      if (ti + kPfStages - 1 < ntiles) load_tile(ti + kPfStages - 1, (ti + kPfStages - 1) % kPfStages);
+      else cp_async_commit();
+      cp_async_wait<kPfStages - 1>();
       __syncthreads();
-      const __nv_bfloat16* buf = tiles + (size_t)(ti & 1) * kPfR * kPfRowPad;
+      const __nv_bfloat16* buf = tiles + (size_t)(ti % kPfStages) * kPfR * kPfRowPad;
       const int c0 = ti * kPfCols;
+      const bool interior = c0 >= lo_max && c0 + kPfCols <= hi_min;
       float acc[2][4];
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb) {
@@ -197,27 +221,27 @@ __global__ void __launch_bounds__(kThreads, 2) prefill_topk_kernel(PrefillParams
       for (int nb = 0; nb < 2; ++nb) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int rr = g + ((e >> 1) << 3);
+          const int h = e >> 1;
+          const int rr = g + 8 * h;
           const int cl = warp * 16 + nb * 8 + 2 * t4 + (e & 1);
           const int c = c0 + cl;
-          if (c < s_lo[rr] || c >= s_hi[rr]) continue;
+          if (!interior && (c < lo2[h] || c >= hi2[h])) continue;
           const uint32_t key = score_key(acc[nb][e]);
-          const int st = s_state[rr];
           if (sweep == 0) {
             if (p.scores) p.scores[((size_t)head * p.T + t0 + rr) * p.C + c] = acc[nb][e];
-            if (st == 1) {
+            if (st2[h] == 1) {
               const uint32_t d = key >> 21;
               atomicAdd(&hist[rr * (kPfBins / 2) + (d >> 1)], 1u << ((d & 1) << 4));
             }
           } else if (sweep < 3) {
-            if (st == 1 && (key >> (sweep == 1 ? 21 : 10)) == s_pref[rr]) {
+            if (st2[h] == 1 && (key >> sh_cmp) == pf2[h]) {
               const uint32_t d = sweep == 1 ? (key >> 10) & 2047u : key & 1023u;
               atomicAdd(&hist[rr * (kPfBins / 2) + (d >> 1)], 1u << ((d & 1) << 4));
             }
           } else {
-            const uint32_t kp = key >> s_shift[rr], pf = s_pref[rr];
-            if (kp > pf) atomicOr(&m_gt[rr * 4 + (cl >> 5)], 1u << (cl & 31));
-            else if (kp == pf && s_need[rr] > 0) atomicOr(&m_eq[rr * 4 + (cl >> 5)], 1u << (cl & 31));
+            const uint32_t kp = key >> sh2[h];
+            if (kp > pf2[h]) atomicOr(&m_gt[rr * 4 + (cl >> 5)], 1u << (cl & 31));
+            else if (kp == pf2[h] && eq2[h]) atomicOr(&m_eq[rr * 4 + (cl >> 5)], 1u << (cl & 31));
           }
         }
       }

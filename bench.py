@@ -60,6 +60,8 @@ def parse():
     ap.add_argument("--context-split", action="store_true",
                     help="C4 measurement: one sequence split over the torchrun ranks (attention_lab_b200.context_split)")
     ap.add_argument("--no-graph", action="store_true", help="context split: launch every step from the host")
+    ap.add_argument("--prefill", action="store_true",
+                    help="C5 measurement: the batched prefill scorer over one 8192-token chunk (8 heads, k=256)")
     return ap.parse_args()
 
 
@@ -298,12 +300,133 @@ def run_context_split(args):
         dist.destroy_process_group()
 
 
+def cpu_prefill_sample(H, T, k, budget_s):
+    """The whole C5 chunk (H heads x T rows) through oracle.cpu_prefill_rows (float32 numpy), blocks of 256 rows in
+    parallel over the host cores (one BLAS thread each); repeated until ~budget_s. Returns query rows/s."""
+    import numpy as np
+    from concurrent.futures import ThreadPoolExecutor
+    from threadpoolctl import threadpool_limits
+    from oracle import oracle as orc
+    rng = np.random.default_rng(0)
+    u = rng.standard_normal((H, T, R), dtype=np.float32)
+    zT = rng.standard_normal((H, R, T), dtype=np.float32)
+    blocks = [(h, t0) for t0 in range(T - 256, -1, -256) for h in range(H)]      # longest rows first
+    workers = max(1, min(64, os.cpu_count() or 1))
+
+    def one(b):
+        h, t0 = b
+        return orc.cpu_prefill_rows(u[h], zT[h], 0, t0, t0 + 256, k)
+    with threadpool_limits(1), ThreadPoolExecutor(workers) as ex:
+        passes, t0 = 0, time.perf_counter()
+        while True:
+            list(ex.map(one, blocks))
+            passes += 1
+            if time.perf_counter() - t0 >= budget_s:
+                break
+        wall = time.perf_counter() - t0
+    return {"value": round(H * T * passes / wall, 1), "unit": "rows/s", "cores": workers, "kind": "port",
+            "sample": f"the whole chunk ({H} heads x {T} rows, float32 matmul + argpartition per row), {passes} "
+                      f"pass(es) in {wall:.1f} s over {workers} threads"}
+
+
+def run_prefill(args):
+    """Config C5: the batched prefill scorer (al_prefill_score_topk) over one chunk of T = 8192 query rows against
+    C = 8192 cached keys, 8 KV heads, r = 32, bf16 ~N(0,1) inputs, causal candidates, top-256 per row. One launch per
+    step; the L2 is flushed (a 256 MiB write) before every timed launch, outside the events. Under torchrun every rank
+    runs its own chunk (replicas, no collective). Prints one JSON line (rank 0)."""
+    import torch
+    import torch.distributed as dist
+    from attention_lab_b200 import ops
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    H, T, C, k = 8, 8192, 8192, 256
+    gen = torch.Generator(device=dev).manual_seed(7 + rank)
+    u = torch.randn(H, T, R, generator=gen, device=dev).to(torch.bfloat16)
+    zT = torch.randn(H, R, C, generator=gen, device=dev).to(torch.bfloat16)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(3, args.warmup)):
+        ops.prefill_score_topk(u, zT, k)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        for e0, e1 in ev:
+            flush.fill_(1)
+            e0.record(stream)
+            ops.prefill_score_topk(u, zT, k)
+            e1.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in ev) / args.steps], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end through the operator: pinned host inputs in, indices back to the host, every step
+    hu, hz = u.cpu().pin_memory(), zT.cpu().pin_memory()
+    hidx = torch.empty((H, T, k), dtype=torch.int32).pin_memory()
+    du, dz = torch.empty_like(u), torch.empty_like(zT)
+
+    def e2e_step():
+        du.copy_(hu, non_blocking=True)
+        dz.copy_(hz, non_blocking=True)
+        hidx.copy_(ops.prefill_score_topk(du, dz, k), non_blocking=True)
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    m = [max(0, min(C, p + 1 - 64) - min(4, p + 1)) for p in range(T)]
+    flops = 2.0 * H * R * sum(m)                          # candidate columns only
+    nbytes = u.numel() * 2 + zT.numel() * 2 + H * T * k * 4
+    hbm, _ = measured_peak()
+    peaks = ROOT / "MEASURED_PEAKS.json"
+    tflops_peak = float(json.loads(peaks.read_text())["bf16_tflops"]) if peaks.exists() else 1590.0
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    line = {"metric": "C5 prefill scorer query rows per second (8 heads x 8192 rows, top-256 each)",
+            "value": round(world * H * T / (ms * 1e-3), 1), "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "C5: batched prefill scorer, u [8,8192,32] x zT [8,32,8192] bf16 N(0,1), causal, "
+                                   "per-row top-256 (int32 positions out)",
+                       "l2": "flushed before every timed launch (256 MiB write)"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "traffic": None, "algorithmic_bytes": nbytes,
+                         "tensor": {"flops": flops, "achieved_tflops": round(flops / (ms * 1e-3) / 1e12, 2),
+                                    "peak_tflops": tflops_peak,
+                                    "frac": round(flops / (ms * 1e-3) / 1e12 / tflops_peak, 5)}},
+            "e2e": {"value": round(world * H * T / (e2e_ms * 1e-3), 1), "unit": "rows/s",
+                    "h2d_bytes_per_step": u.numel() * 2 + zT.numel() * 2, "d2h_bytes_per_step": H * T * k * 4},
+            "gpu_launches": args.steps, "clocks": clocks.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_prefill_sample(H, T, k, args.cpu_seconds)
+    if rank == 0:
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return run_reference_arm(args)
     if args.context_split:
         return run_context_split(args)
+    if args.prefill:
+        return run_prefill(args)
     import torch
     import torch.distributed as dist
     import attention_lab_b200 as al

@@ -461,3 +461,23 @@ def cpu_sparse_request(q, q_pre, K, V, zT, wq_t, wk, k_new, lo: int, hi: int, k:
         p /= p.sum(axis=1, keepdims=True)
         out[g] = p @ vs
     return out
+
+
+def cpu_prefill_rows(u: np.ndarray, zT: np.ndarray, q_pos0: int, t0: int, t1: int, k: int) -> np.ndarray:
+    """float32 timing restatement of prefill_topk for query rows [t0, t1) of one head (u [T,r], zT [r,C]): one
+    matmul for the block, then a partial sort per row (np.argpartition; ties are not ordered here, this is the CPU
+    baseline's cost model, not a parity oracle). Returns int32 [t1-t0, k]."""
+    hi_max = max(0, q_pos0 + t1 - 64)
+    s_all = u[t0:t1] @ zT[:, :hi_max]
+    out = np.full((t1 - t0, k), -1, dtype=np.int32)
+    for i in range(t1 - t0):
+        L = q_pos0 + t0 + i + 1
+        lo = min(4, L)
+        hi = max(lo, L - 64)
+        kk = min(k, hi - lo)
+        if kk == 0:
+            continue
+        s = s_all[i, lo:hi]
+        part = np.argpartition(-s, kk - 1)[:kk] if kk < hi - lo else np.arange(hi - lo)
+        out[i, :kk] = np.sort(part) + lo
+    return out
