@@ -14,7 +14,9 @@ scores, top-k, F merge, gather-free attention). Every layer has its own cache, s
 Under torchrun every rank runs the same per-GPU workload on its own requests (request sharding, no collective on
 the data path: weak scaling); the timed region is bracketed by barriers and synchronisations, its device time is the
 max over ranks, and rank 0 prints one JSON line. `--impl reference` times the CPU restatement of the reference's
-path (oracle/oracle.py) on the host cores and prints the reference arm's line.
+path (oracle/oracle.py) on the host cores and prints the reference arm's line. Two other measurements print their
+own line: `--context-split` (C4, one sequence split over the torchrun ranks) and `--prefill` (C5, the batched
+prefill scorer over one 8192-token chunk).
 """
 from __future__ import annotations
 
