@@ -111,7 +111,8 @@ class CudaContextOps:
         dev = q_pre.device
         return _ops.context_local_topk(q_pre, zT, wq_t_scaled, wk, plan.fixed_rows(B, G, dev), plan.off_lo(B, G, dev),
                                        plan.lo, plan.hi, plan.k_local, key_pos=plan.start, key_stride=plan.k,
-                                       k_pre_new=k_pre_new, write_col=plan.write_col)
+                                       k_pre_new=k_pre_new if plan.write_col >= 0 else None,
+                                       write_col=plan.write_col)
 
     @staticmethod
     def threshold(all_keys, rows, plan: ShardPlan):
@@ -139,14 +140,18 @@ def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, 
                               group=None, k_pre_new=None, scale=None, ops=None):
     """One layer's sparse decode step with the sequence split over the group's ranks (this rank holds the shard of
     `plan`: caches [B,G,shard_capacity,d] and zT [B,G,r,shard_capacity]). Every rank calls it with the same global
-    step and gets the full output [B,G,h,1,d]; it equals decode.py:145-163 run on the unsplit caches."""
+    step and gets the full output [B,G,h,1,d]; it equals decode.py:145-163 run on the unsplit caches. `k_pre_new`
+    ([B,G,1,d], the newest key before RoPE) may be given on every rank: the rank whose shard holds position
+    legal_length - 1 writes its index column, the others ignore it."""
     ops = CudaContextOps if ops is None else ops
     world = plan.world
     if world > 1 and dist.get_world_size(group) != world:
         raise ValueError(f"plan is for {world} ranks, the group has {dist.get_world_size(group)}")
     B, G, h, _, d = q_main.shape
+    # every rank may pass the newest key's pre-RoPE features; only the shard that owns position L - 1 writes its z
+    kpn = k_pre_new if plan.write_col >= 0 else None
     if plan.selected_count > 0:
-        rows, keys = ops.local_topk(q_pre, zT, wq_t_scaled, wk, plan, k_pre_new=k_pre_new)
+        rows, keys = ops.local_topk(q_pre, zT, wq_t_scaled, wk, plan, k_pre_new=kpn)
     else:   # a shard past the legal range: nothing to score, nothing to attend
         rows = torch.empty((B, G, 0), dtype=torch.int64, device=q_main.device)
         keys = torch.zeros((B, G, plan.k), dtype=torch.int64, device=q_main.device)

@@ -627,6 +627,8 @@ int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const v
                                              (long long)q_pos0 + T, C);
   if ((long long)q_pos0 + T > 65536) return fail(AL_EUNSUPPORTED, "legal lengths above 65536 are not supported");
   if (k < 0 || kcap < k) return fail(AL_EINVAL, "need 0 <= k <= kcap (k=%d, kcap=%d)", k, kcap);
+  // a row never has more candidates than its legal length (at most 65536 here), so larger slots could never be filled
+  if (kcap > C || kcap > 65536) return fail(AL_EINVAL, "kcap=%d exceeds min(C=%d, 65536)", kcap, C);
   if (C % 8 || z_ld % 8 || z_sh % 8 || (reinterpret_cast<uintptr_t>(zT) & 15))
     return fail(AL_EUNSUPPORTED, "zT needs 16-byte aligned rows (C, row and head strides multiples of 8)");
   if (z_ld < C || u_st < kPfR) return fail(AL_EINVAL, "strides smaller than the rows they step over");

@@ -20,7 +20,8 @@ _SAVED = "_attention_lab_b200_saved"
 
 def _append(self, layer: int, k_main, v, z=None) -> None:
     """LabCache.append with the reference's contract (one append per layer per forward, equal lengths within a
-    forward, capacity check) and the copies done by al_append_kvz."""
+    forward, capacity check) and the copies done by al_append_kvz. As in the reference, K and V are written before a
+    z for a cache without an index table raises RuntimeError (the cache then holds the new K/V rows, uncounted)."""
     start, T = self.valid_length, int(k_main.shape[2])
     if start + T > self.capacity:
         raise RuntimeError(f"cache capacity {self.capacity} exceeded: valid {start} + new {T}")
@@ -29,6 +30,7 @@ def _append(self, layer: int, k_main, v, z=None) -> None:
     elif self._pending != T:
         raise RuntimeError("layers appended different lengths within one forward")
     if z is not None and self.z is None:
+        ops.append_kvz(self.k[layer], self.v[layer], None, start, k_main, v)
         raise RuntimeError("this cache was created without an index table")
     ops.append_kvz(self.k[layer], self.v[layer], None if z is None else self.z[layer], start, k_main, v,
                    None if z is None else z.to(self.z[layer].dtype))

@@ -253,10 +253,8 @@ def run_context_split(args):
     K, V, Z = rnd(B, G, cs_, D), rnd(B, G, cs_, D), rnd(B, G, R, cs_, scale=0.23)
     WQ, WK = rnd(G, h * D, R, scale=0.02 / math.sqrt(R)), rnd(G, R, D, scale=0.02)
     Q, QP, KPN = rnd(B, G, h, 1, D), rnd(B, G, h, 1, D), rnd(B, G, 1, D)
-    kpn = KPN if plan.write_col >= 0 else None
-
-    def step():
-        return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=kpn)
+    def step():    # every rank passes the newest key; the shard that owns position L - 1 writes its z column
+        return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=KPN)
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):

@@ -80,3 +80,25 @@ def check_scores(got, want64, what="scores"):
     rel = np.linalg.norm(got - want64) / (np.linalg.norm(want64) + 1e-30)
     assert diff.max() <= F32_SCORES["atol"], f"{what}: max |diff| {diff.max():.3e}"
     assert rel <= F32_SCORES["rel_norm"], f"{what}: rel norm {rel:.3e}"
+
+
+def check_topk_float64(chosen, scores64, k, what="top-k"):
+    """chosen [..., k] candidate indices (any order) against the float64 top-k of scores64 [..., M] under
+    (score desc, index asc): the sets must be equal except for candidates whose float64 score lies within TIE_TOL
+    (relative to max(1, |k-th score|)) of the k-th score -- the north-star rule for identical inputs computed in
+    fp32. Returns the number of segments whose sets differ (inside the tolerance)."""
+    from oracle import oracle as orc
+    chosen = np.asarray(chosen)
+    s = np.asarray(scores64, dtype=np.float64)
+    want = orc.topk_indices(s, k)
+    kth = np.sort(s, axis=-1)[..., ::-1][..., k - 1]
+    n_diff = 0
+    for idx in np.ndindex(*s.shape[:-1]):
+        diff = set(chosen[idx].tolist()) ^ set(want[idx].tolist())
+        assert len(set(chosen[idx].tolist())) == k, f"{what} {idx}: duplicate or missing candidates"
+        for m in diff:
+            assert abs(s[idx][m] - kth[idx]) <= TIE_TOL * max(1.0, abs(kth[idx])), \
+                f"{what} {idx}: candidate {m} (score {s[idx][m]:.9g}) differs from the float64 top-k " \
+                f"(k-th {kth[idx]:.9g}) beyond the tie tolerance"
+        n_diff += len(diff) > 0
+    return n_diff

@@ -66,8 +66,10 @@ class OracleOps:
         self.wq_t = wq_t
 
     def local_topk(self, q_pre, zT, wq_t_scaled, wk, plan, *, k_pre_new=None):
-        assert k_pre_new is None
         B, G = q_pre.shape[:2]
+        if k_pre_new is not None:       # the z column of the newest key (decode.py:156-157), owning shard only
+            assert plan.write_col >= 0, "k_pre_new reached a shard that does not own position L - 1"
+            zT[..., plan.write_col] = torch.from_numpy(orc.project_keys(k_pre_new.numpy(), wk.numpy())[..., 0])
         u = orc.project_queries(q_pre.numpy(), wq_t_scaled.numpy())
         s = _scores32(u, zT.numpy(), plan.lo, plan.hi)                       # [B,G,M_local]
         pos = plan.start + np.arange(plan.lo, plan.hi)
@@ -129,7 +131,9 @@ def _problem(seed, B, G, h, d, r, C, L, mirror=False):
     if mirror:                                        # every score has a twin half a sequence later
         zT[..., L // 2:L] = zT[..., :L - L // 2]
     wq_t = (rng.standard_normal((G, h * d, r)) * 0.02).astype(np.float32)
-    return q, q_pre, K, V, zT, wq_t
+    wk = (rng.standard_normal((G, r, d)) * 0.02).astype(np.float32)
+    k_pre_new = rng.standard_normal((B, G, 1, d)).astype(np.float32)
+    return q, q_pre, K, V, zT, wq_t, wk, k_pre_new
 
 
 def _single_device(q, q_pre, K, V, zT, wq_t, L, k0):
@@ -156,7 +160,7 @@ def _worker(rank, world, port, cap, L, mirror, result_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
         B, G, h, d, r = 1, 2, 2, 128, 32
-        q, q_pre, K, V, zT, wq_t = _problem(7, B, G, h, d, r, cap, L, mirror)
+        q, q_pre, K, V, zT, wq_t, wk, k_pre_new = _problem(7, B, G, h, d, r, cap, L, mirror)
         k0 = fixed_budget(L, 1 / 16)
         plan = csplit.plan_shard(L, k0, rank, world, cap)
         cs_, st = plan.shard_capacity, plan.start
@@ -166,10 +170,13 @@ def _worker(rank, world, port, cap, L, mirror, result_dir):
             x = np.concatenate([x, np.zeros(x.shape[:axis] + (pad,) + x.shape[axis + 1:], x.dtype)], axis=axis)
             return torch.from_numpy(np.ascontiguousarray(np.take(x, range(st, st + cs_), axis=axis)))
         ops = OracleOps(wq_t)
+        z_shard = shard(zT, 3)
+        # every rank passes the newest key; the protocol lets only the owner of position L - 1 write its z column
         out = csplit.context_split_decode_step(torch.from_numpy(q), torch.from_numpy(q_pre), shard(K, 2), shard(V, 2),
-                                               shard(zT, 3), torch.from_numpy(wq_t), None, plan, ops=ops,
-                                               scale=1 / math.sqrt(d))
+                                               z_shard, torch.from_numpy(wq_t), torch.from_numpy(wk), plan, ops=ops,
+                                               k_pre_new=torch.from_numpy(k_pre_new), scale=1 / math.sqrt(d))
         np.save(os.path.join(result_dir, f"out{rank}.npy"), out.numpy())
+        np.save(os.path.join(result_dir, f"z{rank}.npy"), z_shard.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -187,8 +194,18 @@ def test_context_split_on_gloo_ranks_equals_single_device(world, cap, L, mirror,
     (world 4 with capacity 2048 leaves two ranks past the legal range, holding nothing; `mirror` makes every
     selection a tie decided by position across shards)."""
     mp.spawn(_worker, args=(world, _free_port(), cap, L, mirror, str(tmp_path)), nprocs=world, join=True)
-    q, q_pre, K, V, zT, wq_t = _problem(7, 1, 2, 2, 128, 32, cap, L, mirror)
+    q, q_pre, K, V, zT, wq_t, wk, k_pre_new = _problem(7, 1, 2, 2, 128, 32, cap, L, mirror)
     want, _ = _single_device(q, q_pre, K, V, zT, wq_t, L, fixed_budget(L, 1 / 16))
+    z_new = orc.project_keys(k_pre_new, wk)[..., 0].astype(np.float32)        # [B,G,r]
     for rank in range(world):
         got = np.load(tmp_path / f"out{rank}.npy")
         assert np.abs(got - want).max() < 1e-10, f"rank {rank}"
+        plan = csplit.plan_shard(L, fixed_budget(L, 1 / 16), rank, world, cap)
+        z_got = np.load(tmp_path / f"z{rank}.npy")
+        z_orig = np.concatenate([zT, np.zeros(zT.shape[:3] + (plan.shard_capacity * world - cap,), zT.dtype)],
+                                axis=3)[..., plan.start:plan.start + plan.shard_capacity]
+        changed = np.nonzero((z_got != z_orig).any(axis=(0, 1, 2)))[0].tolist()
+        if plan.write_col >= 0:
+            assert changed in ([plan.write_col], []) and np.array_equal(z_got[..., plan.write_col], z_new)
+        else:
+            assert changed == [], f"rank {rank} does not own position L - 1 but changed its index table"

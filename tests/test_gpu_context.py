@@ -19,7 +19,7 @@ import pytest
 import torch
 
 from oracle import oracle as orc
-from parity import check_out
+from parity import check_out, check_topk_float64
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -75,7 +75,7 @@ def _emulate(t, L, k0, world, cap):
         K, V, zT = shard(t["k"], 2, p), shard(t["v"], 2, p), shard(t["zT"], 3, p)
         if p.selected_count > 0:
             rows, keys = csplit.CudaContextOps.local_topk(t["q_pre"], zT, t["wq_t"], t["wk"], p,
-                                                          k_pre_new=t["k_pre_new"] if p.write_col >= 0 else None)
+                                                          k_pre_new=t["k_pre_new"])     # gated by the plan
         else:
             rows = torch.empty(B, G, 0, dtype=torch.int64, device=DEV)
             keys = torch.zeros(B, G, p.k, dtype=torch.int64, device=DEV)
@@ -117,7 +117,7 @@ def test_context_split_kernels_equal_the_fused_step(world, cap, L, mirror):
     """(4, 12288, 8192): the last rank lies past the legal range; (8, 4096, 3600): F's recent window [3536, 3600)
     straddles the last shard boundary, so the last shard holds F rows and no candidate (k_local = 0)."""
     from attention_lab_b200 import _lib
-    from attention_lab_b200.selection import fixed_budget
+    from attention_lab_b200.selection import fixed_budget, selection_layout
     k0 = fixed_budget(L, 1 / 32)
     t = _inputs(2, 8, 4, cap, L, seed=world * 10 + int(mirror), mirror=mirror)
     out_f, pos_f, zT_f = _fused(t, L, k0)
@@ -127,6 +127,12 @@ def test_context_split_kernels_equal_the_fused_step(world, cap, L, mirror):
     for b in range(B):
         for g in range(G):
             assert kept[b][g] == set(pos_f[b, g].tolist()), f"segment ({b},{g})"
+    # the fused rows (and so the kept rows) against the float64 oracle's top-k of the same inputs
+    lay = selection_layout(L)
+    f64 = lambda x: x.double().cpu().numpy()
+    u64 = orc.project_queries(f64(t["q_pre"]), f64(t["wq_t"]))
+    s64 = orc.candidate_scores(u64, f64(t["zT"]), lay.candidate_lo, lay.candidate_hi)[:, :, 0, :]
+    check_topk_float64(pos_f[..., lay.fixed_count:] - lay.candidate_lo, s64, lay.clamp_k(k0), "split top-k")
     # the newest key's z column, written by the shard that owns position L-1
     owner = [p for p in plans if p.write_col >= 0][0]
     zc = zT_sh[owner.rank][..., owner.write_col]
@@ -172,8 +178,7 @@ def _nccl_worker(rank, world, port, L, cap, result_dir):
         cs_ = plan.shard_capacity
         sl = lambda x, dim: x.narrow(dim, plan.start, cs_).contiguous()
         out = csplit.context_split_decode_step(t["q"], t["q_pre"], sl(t["k"], 2), sl(t["v"], 2), sl(t["zT"], 3),
-                                               t["wq_t"], t["wk"], plan,
-                                               k_pre_new=t["k_pre_new"] if plan.write_col >= 0 else None)
+                                               t["wq_t"], t["wk"], plan, k_pre_new=t["k_pre_new"])
         torch.cuda.synchronize()
         np.save(os.path.join(result_dir, f"out{rank}.npy"), out.float().cpu().numpy())
     finally:

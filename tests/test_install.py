@@ -50,13 +50,28 @@ def test_append_keeps_the_reference_contract():
         c = m.LabCache(capacity=4)
         with pytest.raises(RuntimeError, match="capacity"):
             c.append(0, torch.zeros(1, 2, 5, 128), torch.zeros(1, 2, 5, 128))
-        with pytest.raises(RuntimeError, match="index table"):
-            c.append(0, torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 32, 1))
         c._pending = 2
         with pytest.raises(RuntimeError, match="different lengths"):
             c.append(0, torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 1, 128))
         c._pending = None
         with pytest.raises(ValueError, match="CUDA"):          # no CPU path behind the kernels
             c.append(0, torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 1, 128))
+    finally:
+        inst.uninstall(m)
+
+
+def test_append_without_index_table_writes_kv_first(monkeypatch):
+    """The reference (qwen_wrap.py:100-104) copies K and V, then raises for a z without an index table; the
+    installed append issues the K/V copy first too, and counts no write."""
+    calls = []
+    monkeypatch.setattr(inst.ops, "append_kvz", lambda *a, **k: calls.append(a))
+    m = fake_wrapper()
+    inst.install(m)
+    try:
+        c = m.LabCache(capacity=4)
+        with pytest.raises(RuntimeError, match="index table"):
+            c.append(0, torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 1, 128), torch.zeros(1, 2, 32, 1))
+        assert len(calls) == 1 and calls[0][2] is None and calls[0][3] == 0     # K/V only, at position 0
+        assert c.writes == [0] and c.last_write == [None]
     finally:
         inst.uninstall(m)
