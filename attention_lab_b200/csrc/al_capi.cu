@@ -87,8 +87,8 @@ int prepare_kernel(K kernel, size_t smem, int cs) {
 
 std::unordered_map<unsigned long long, int> g_cluster_ok;   // (kernel, cs, smem, device) -> schedulable
 
-template <typename K, typename P>
-int launch(K kernel, dim3 grid, int cs, size_t smem, void* stream, const P& p) {
+template <typename K, typename... P>
+int launch(K kernel, dim3 grid, int cs, size_t smem, void* stream, const P&... p) {
   int rc = prepare_kernel(kernel, smem, cs);
   if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
@@ -124,7 +124,7 @@ int launch(K kernel, dim3 grid, int cs, size_t smem, void* stream, const P& p) {
     }
     if (!ok) return fail(AL_EUNSUPPORTED, "a cluster of %d CTAs with %zu bytes of shared memory cannot be scheduled", cs, smem);
   }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, p...);
   if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx");
   return AL_OK;
 }
@@ -176,20 +176,64 @@ int auto_cluster(int segs, int M, int sms, int max_keys) {
 }
 
 template <typename KV_T, typename IDX_T>
-int dispatch_fused_h(const DecodeParams& p, int hp, dim3 grid, int cs, size_t smem, void* stream) {
+int dispatch_fused_h(const DecodeParams& p, const CUtensorMap& zmap, int hp, dim3 grid, int cs, size_t smem,
+                     void* stream) {
   switch (hp) {
-    case 1: return launch(sparse_step_kernel<KV_T, IDX_T, 1>, grid, cs, smem, stream, p);
-    case 2: return launch(sparse_step_kernel<KV_T, IDX_T, 2>, grid, cs, smem, stream, p);
-    default: return launch(sparse_step_kernel<KV_T, IDX_T, 4>, grid, cs, smem, stream, p);
+    case 1: return launch(sparse_step_kernel<KV_T, IDX_T, 1>, grid, cs, smem, stream, p, zmap);
+    case 2: return launch(sparse_step_kernel<KV_T, IDX_T, 2>, grid, cs, smem, stream, p, zmap);
+    default: return launch(sparse_step_kernel<KV_T, IDX_T, 4>, grid, cs, smem, stream, p, zmap);
   }
 }
 
-int dispatch_fused(const DecodeParams& p, int kv_dtype, int idx_dtype, int hp, dim3 grid, int cs, size_t smem,
-                   void* stream) {
-  if (kv_dtype == AL_BF16 && idx_dtype == AL_F32) return dispatch_fused_h<__nv_bfloat16, float>(p, hp, grid, cs, smem, stream);
-  if (kv_dtype == AL_BF16 && idx_dtype == AL_BF16) return dispatch_fused_h<__nv_bfloat16, __nv_bfloat16>(p, hp, grid, cs, smem, stream);
-  if (kv_dtype == AL_F32 && idx_dtype == AL_F32) return dispatch_fused_h<float, float>(p, hp, grid, cs, smem, stream);
-  return dispatch_fused_h<float, __nv_bfloat16>(p, hp, grid, cs, smem, stream);
+int dispatch_fused(const DecodeParams& p, const CUtensorMap& zmap, int kv_dtype, int idx_dtype, int hp, dim3 grid,
+                   int cs, size_t smem, void* stream) {
+  if (kv_dtype == AL_BF16 && idx_dtype == AL_F32)
+    return dispatch_fused_h<__nv_bfloat16, float>(p, zmap, hp, grid, cs, smem, stream);
+  if (kv_dtype == AL_BF16 && idx_dtype == AL_BF16)
+    return dispatch_fused_h<__nv_bfloat16, __nv_bfloat16>(p, zmap, hp, grid, cs, smem, stream);
+  if (kv_dtype == AL_F32 && idx_dtype == AL_F32) return dispatch_fused_h<float, float>(p, zmap, hp, grid, cs, smem, stream);
+  return dispatch_fused_h<float, __nv_bfloat16>(p, zmap, hp, grid, cs, smem, stream);
+}
+
+// Tensor map of an index table zT [B,G,r,C] viewed as [B*G*r rows, C columns] with boxes of 32 rows x 512 bytes
+// (the resident-key scan's tiles). The driver's encoder is reached through the runtime (no libcuda link); maps are
+// cached by (address, shape, dtype). Returns false when the encoder is unavailable or refuses the layout.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+std::unordered_map<unsigned long long, CUtensorMap> g_zmaps;
+
+bool zt_tensor_map(const void* zT, int idx_dtype, long long rows, int C, CUtensorMap* out) {
+  static EncodeTiledFn enc = nullptr;
+  static bool tried = false;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!tried) {
+    tried = true;
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      enc = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  if (!enc) return false;
+  const unsigned long long key = reinterpret_cast<unsigned long long>(zT) ^ ((unsigned long long)C << 1) ^
+                                 ((unsigned long long)rows << 29) ^ ((unsigned long long)idx_dtype << 62);
+  auto it = g_zmaps.find(key);
+  if (it != g_zmaps.end()) { *out = it->second; return true; }
+  const int es = esize(idx_dtype);
+  cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)C * (cuuint64_t)es};
+  cuuint32_t box[2] = {(cuuint32_t)(512 / es), 32u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUtensorMap m;
+  const CUresult r = enc(&m, idx_dtype == AL_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                         const_cast<void*>(zT), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (g_zmaps.size() > 4096) g_zmaps.clear();
+  g_zmaps[key] = m;
+  *out = m;
+  return true;
 }
 
 int dispatch_attend(const AttendParams& p, int kv_dtype, int hp, dim3 grid, int cs, size_t smem, void* stream) {
@@ -253,10 +297,18 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
 
   const int hp = attend ? pad_heads(p.h) : 1;
   const int budget = di->max_smem_optin - kFusedStaticBytes;
-  // Shared memory per CTA: the selection region [histogram | cluster slice | bitmaps | candidate list] aliased with
-  // the attend engine, then the attend row list. The candidate list takes whatever the engine leaves, and at least
-  // room for a typical filtered list (the first scan round, plus about ln(columns / round) * k later keys). The
-  // cluster size is the automatic (or requested) one, grown while a CTA's share does not fit.
+  // Resident-key scan (select_mode 1, r = 32, 16-byte aligned index rows, a tensor map): the index tiles stream
+  // through a ring of 16 KB stages placed after the histogram (and the cluster slice), inside the attend engine's
+  // footprint; every key goes to TMEM, so there is no candidate list. After the scan the bitmaps (and the per-column
+  // keys of keys_out) reuse the ring. Otherwise: [histogram | cluster slice | bitmaps | candidate list].
+  CUtensorMap zmap;
+  std::memset(&zmap, 0, sizeof(zmap));
+  const bool tk_ok = p.select_mode == 1 && p.scan && p.r == kMaxR && p.zvec &&
+                     zt_tensor_map(p.zT, idx_dtype, (long long)p.B * p.G * p.r, p.C, &zmap);
+  // Shared memory per CTA: the selection region aliased with the attend engine, then the attend row list. The list
+  // path's candidate list takes whatever the engine leaves, and at least room for a typical filtered list (the first
+  // scan round, plus about ln(columns / round) * k later keys). The cluster size is the automatic (or requested) one,
+  // grown while a CTA's share does not fit.
   int cs = cluster > 0 ? cluster : auto_cluster(p.B * p.G, p.M, di->sms, 1 << 30);
   if (cs < 1 || cs > kMaxCluster) return fail(AL_EINVAL, "cluster must be in [1, %d], got %d", kMaxCluster, cs);
   const int round_cols = kThreads * (p.zvec ? 16 / ez : 1);
@@ -266,13 +318,22 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
     if (p.cpc == 0) p.cpc = 8;
     size_t sel_fixed = 0;
     int cap_min = 0;
+    p.tkeys = tk_ok && p.cpc + 32 <= kTkeyMaxCols ? 1 : 0;
     if (p.select_mode == 1) {
       if (p.cpc > 65535) { if (cluster > 0 || cs >= kMaxCluster) return fail(AL_EUNSUPPORTED, "more than 65535 candidates per CTA (cluster %d)", cs); continue; }
       p.nwp = (p.cpc + 30) / 32 + 1;
-      p.bm_off = 4096 * 4 + (cs > 1 ? (int)round_up((size_t)(4096 / cs) * 4, 16) : 0);
-      p.list_off = p.bm_off + (int)round_up((size_t)p.nwp * 8, 16);
-      sel_fixed = (size_t)p.list_off;
-      cap_min = std::min(p.cpc, round_cols + 6 * p.k + 1024);
+      const int slice = cs > 1 ? (int)round_up((size_t)(4096 / cs) * 4, 16) : 0;
+      if (p.tkeys) {
+        // during the scan: [packed histogram 8 KB | ring]; after it: [histogram | cluster slice | bitmaps]
+        p.ring_off = 2048 * 4;
+        p.bm_off = 4096 * 4 + slice;
+        sel_fixed = (size_t)p.bm_off + round_up((size_t)p.nwp * 8, 16);
+      } else {
+        p.bm_off = 4096 * 4 + slice;
+        p.list_off = p.bm_off + (int)round_up((size_t)p.nwp * 8, 16);
+        sel_fixed = (size_t)p.list_off;
+        cap_min = std::min(p.cpc, round_cols + 6 * p.k + 1024);
+      }
     }
     const int rows_cap = (p.F + cs - 1) / cs + (p.k < p.cpc ? p.k : p.cpc) + 8;
     // the deepest pipeline that leaves room for two CTAs per SM, else the deepest that fits at all
@@ -281,16 +342,32 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
     for (int st = kFusedStages; st >= 3 && !fits; --st) {
       const size_t eng = attend ? (size_t)engine_smem(kv_dtype, hp, st) : 0;
       p.cap = 0;
-      if (p.select_mode == 1) {
+      size_t select_bytes = sel_fixed;
+      if (p.select_mode == 1 && !p.tkeys) {
         const size_t room = eng > sel_fixed ? (eng - sel_fixed) / 8 : 0;
         p.cap = (int)std::min<size_t>((size_t)p.cpc, std::max<size_t>(room, (size_t)cap_min));
+        select_bytes += (size_t)p.cap * 8;
       }
-      size_t select_bytes = sel_fixed + (size_t)p.cap * 8;
       if (p.keys_out) {                     // per-column keys of the chosen candidates
         p.skey_off = (int)round_up(select_bytes, 16);
         select_bytes = (size_t)p.skey_off + (size_t)(p.cpc + 64) * 4;
       }
-      p.union_bytes = (int)round_up(select_bytes > eng ? select_bytes : eng, 128);
+      size_t region = select_bytes > eng ? select_bytes : eng;
+      if (p.tkeys) {
+        // an even number of ring stages (each half of the CTA owns every other one): as many as the region holds,
+        // up to kMaxRing, and kMaxRing when nothing else sets the size; the launch also keeps above a third of the
+        // SM's shared memory so at most two CTAs share an SM (each holds half of its TMEM columns)
+        p.nring = (int)std::min<size_t>(kMaxRing, region > (size_t)p.ring_off ? (region - p.ring_off) / kTileBytes : 0);
+        if (!attend) p.nring = kMaxRing;
+        p.nring &= ~1;
+        if (p.nring < 2) p.nring = 2;
+        region = std::max(region, (size_t)p.ring_off + (size_t)p.nring * kTileBytes);
+        region = std::max(region, (size_t)80 * 1024);
+        // after the scan, the candidate list of the one-CTA select (keys of the pivot bin and above) takes the rest
+        p.list_off = (int)round_up(select_bytes, 16);
+        p.cap = region > (size_t)p.list_off ? (int)((region - (size_t)p.list_off) / 8) : 0;
+      }
+      p.union_bytes = (int)round_up(region, 128);
       smem = (size_t)p.union_bytes + (size_t)rows_cap * 4;
       p.nstage = st;
       fits = (long long)smem <= (pass == 0 ? kHalfSmBudget : budget);
@@ -302,7 +379,7 @@ int run_fused(DecodeParams p, int kv_dtype, int idx_dtype, int d, int cluster, v
   p.err = di->err;
   dim3 grid((unsigned)cs, (unsigned)(p.B * p.G), 1);
   if (!attend) { p.out = nullptr; p.part = nullptr; }
-  return dispatch_fused(p, attend ? kv_dtype : AL_BF16, idx_dtype, hp, grid, cs, smem, stream);
+  return dispatch_fused(p, zmap, attend ? kv_dtype : AL_BF16, idx_dtype, hp, grid, cs, smem, stream);
 }
 
 }  // namespace

@@ -18,6 +18,7 @@
 // merges the partial softmax states (log-sum-exp) into the output. Nothing is written to global memory except the
 // z column, the output, and the optional row list and scores.
 #pragma once
+#include <cuda.h>
 #include "al_attend.cuh"
 
 namespace al {
@@ -56,6 +57,8 @@ struct DecodeParams {
   long long key_pos;                                // position of column 0 in the keys (a shard's first position)
   int kst;                                          // keys_out entries per segment (>= k; the rest are zero)
   int skey_off;                                     // selection region: per-column keys (keys_out only)
+  int tkeys;                                        // 1: resident-key scan (TMA tiles, keys in TMEM; select_mode 1)
+  int ring_off, nring;                              // resident-key scan: ring offset in dynamic smem, stages
   unsigned* err;                                    // device error word
 };
 
@@ -186,6 +189,191 @@ __device__ __forceinline__ void fma_rows8(float2 (&acc2)[V16<IDX_T>::n / 2], con
 struct NoPre {
   __device__ __forceinline__ void operator()() const {}
 };
+
+// ------------------------------------------------------------------------------------ resident-key scan (TMA + TMEM)
+// The segment's index columns [a0, c1) (a0 = c0 rounded down to 32) stream through shared memory as 2-D bulk-copy
+// tiles of 32 rows x TW columns (16 KB: TW = 256 bf16 or 128 fp32 columns) in an NS-stage ring. A round is two tiles:
+// threads 0-127 take the even tile, 128-255 the odd one; thread pp = tid % 128 of a half owns CPT adjacent columns
+// (CPT = 2 bf16, 1 fp32: a 4-byte word per index row) and accumulates their scores over the 32 rows in ascending
+// order with fp32 FMAs -- the arithmetic of scan_columns, so every key is bit-identical to the other scan paths.
+// Every key goes to tensor memory (the CTA allocates 256 columns; the thread's lane, columns 128 half + CPT round + e),
+// so the exact radix select afterwards re-reads all of them from TMEM instead of the index table: up to 32768 columns
+// per CTA, no candidate list, no rescan. A column outside the CTA's candidates [c0, c1) stores key 0, which no score
+// produces (keys below 0x00800000 would be NaN bit patterns, and NaN maps to 0xffffffff): every bin the select asks
+// about is at least 7, so a key that passes its bin test is a valid candidate without further checks.
+constexpr int kTileBytes = 16384;
+constexpr int kMaxRing = 6;
+constexpr uint32_t kTmemCols = 256;
+constexpr int kTkeyMaxCols = 32768;            // columns [a0, c1) one CTA can hold in TMEM
+
+template <typename IDX_T>
+struct TKeyGeo {
+  static constexpr int CPT = sizeof(IDX_T) == 2 ? 2 : 1;     // columns per thread per tile
+  static constexpr int TW = 128 * CPT;                       // columns per tile
+  static constexpr int ROWB = TW * (int)sizeof(IDX_T);       // bytes per tile row (512)
+  int a0, c0, c1, ntiles, nrounds, nkeys, half, pp;
+  uint32_t tlane;                                            // TMEM address of the thread's first key
+  __device__ __forceinline__ TKeyGeo(int c0_, int c1_, uint32_t tbase) : c0(c0_), c1(c1_) {
+    a0 = (c0 / 32) * 32;                                     // the selection bitmaps' first column: whole words
+    ntiles = c1 > c0 ? (c1 - a0 + TW - 1) / TW : 0;
+    nrounds = (ntiles + 1) / 2;
+    nkeys = nrounds * CPT;
+    half = threadIdx.x >> 7;
+    pp = threadIdx.x & 127;
+    tlane = tbase + ((uint32_t)(32 * ((threadIdx.x >> 5) & 3)) << 16) + 128u * (uint32_t)half;
+  }
+  // column of key i of this thread
+  __device__ __forceinline__ int col(int i) const { return a0 + (2 * (i / CPT) + half) * TW + CPT * pp + i % CPT; }
+  // f(keys[8], i0) for each chunk of 8 of this thread's keys (key i0 + e in keys[e]; entries past the thread's keys
+  // read as 0, like a column outside the candidates); every thread of the CTA calls it (warp-collective loads)
+  template <typename F>
+  __device__ __forceinline__ void for_each_chunk(F&& f) const {
+    for (int q = 0; q * 8 < nkeys; ++q) {
+      uint32_t r[8];
+      tmem_ld8(tlane + 8u * q, r);
+      tmem_wait_ld();
+      if (8 * q + 8 > nkeys) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) r[e] = 8 * q + e < nkeys ? r[e] : 0u;
+      }
+      f(r, 8 * q);
+    }
+  }
+};
+
+// Spread the low 16 bits of x to the even bit positions.
+__device__ __forceinline__ uint32_t spread16(uint32_t x) {
+  x &= 0xffffu;
+  x = (x | (x << 8)) & 0x00ff00ffu;
+  x = (x | (x << 4)) & 0x0f0f0f0fu;
+  x = (x | (x << 2)) & 0x33333333u;
+  return (x | (x << 1)) & 0x55555555u;
+}
+
+// The selection marks from the keys in TMEM: bit (column - a0) of gt / eq for key > tau / key == tau. A warp's keys of
+// one round cover whole bitmap words (a0 is a multiple of 32): 32 consecutive columns (fp32 index) or 64 columns
+// (bf16: the even and odd columns of 32 lanes, interleaved), so each word is built from warp votes and written once
+// with a plain store -- no atomics, no divergence. Words at or beyond nwp are not written (their columns lie past
+// the CTA's candidates). Keys of chosen columns also go to skey[column - a0] when skey is given.
+template <typename IDX_T>
+__device__ void tkey_marks(const TKeyGeo<IDX_T>& g, uint32_t tau, uint32_t* gt, uint32_t* eq, int nwp,
+                           uint32_t* skey) {
+  using Geo = TKeyGeo<IDX_T>;
+  const int lane = threadIdx.x & 31, wq = (threadIdx.x >> 5) & 3;
+  g.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
+    if (Geo::CPT == 2) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int t = 2 * (i0 / 2 + j) + g.half;
+        const uint32_t g0 = __ballot_sync(0xffffffffu, r[2 * j] > tau);
+        const uint32_t g1 = __ballot_sync(0xffffffffu, r[2 * j + 1] > tau);
+        const uint32_t e0 = __ballot_sync(0xffffffffu, r[2 * j] == tau);
+        const uint32_t e1 = __ballot_sync(0xffffffffu, r[2 * j + 1] == tau);
+        const int wi = 8 * t + 2 * wq + (lane >> 4), sh = lane & 16;
+        if ((lane & 15) == 0 && t < g.ntiles && wi < nwp) {
+          gt[wi] = spread16(g0 >> sh) | (spread16(g1 >> sh) << 1);
+          eq[wi] = spread16(e0 >> sh) | (spread16(e1 >> sh) << 1);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int t = 2 * (i0 + e) + g.half;
+        const uint32_t gw = __ballot_sync(0xffffffffu, r[e] > tau);
+        const uint32_t ew = __ballot_sync(0xffffffffu, r[e] == tau);
+        const int wi = 4 * t + wq;
+        if (lane == 0 && t < g.ntiles && wi < nwp) { gt[wi] = gw; eq[wi] = ew; }
+      }
+    }
+    if (skey) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (r[e] >= tau) skey[g.col(i0 + e) - g.a0] = r[e];
+    }
+  });
+}
+
+// Issue tile t of the CTA's columns into ring stage t % nring.
+template <typename IDX_T>
+__device__ __forceinline__ void tkey_issue(const TKeyGeo<IDX_T>& g, const void* map, unsigned char* ring,
+                                           uint64_t* full, int nring, int seg_row, int t) {
+  const int s = t % nring;
+  mbar_arrive_expect_tx(&full[s], kTileBytes);
+  tma_load_2d(ring + s * kTileBytes, map, g.a0 + t * g.TW, seg_row, &full[s]);
+}
+
+// Named barrier of one half of the CTA (threads 128 h .. 128 h + 127; ids 1 and 2).
+__device__ __forceinline__ void half_sync(int half) {
+  asm volatile("bar.sync %0, 128;\n" ::"r"(1 + half) : "memory");
+}
+
+// The scan proper (after tkey_issue of the first min(nring, ntiles) tiles and with u in s_u): scores -> keys -> 12-bit
+// histogram (s_hp: 2048 words, bins 2i and 2i+1 in the low and high 16 bits of word i; a CTA has at most 32768 keys,
+// so no count overflows its half), optional fp32 scores (so, indexed by column), keys to TMEM. The two halves run
+// independently: nring is even, so half h only ever waits on and refills the stages of its own tiles (t = h mod 2),
+// and its leader thread re-arms a stage as soon as the half's 128 threads have read it. Returns false if a bounded
+// wait gave up.
+template <typename IDX_T>
+__device__ __noinline__ bool tkey_scan(const TKeyGeo<IDX_T>& g, const void* map, unsigned char* ring, uint64_t* full, int nring,
+                          int seg_row, const float* s_u, unsigned* s_hp, float* so) {
+  using Geo = TKeyGeo<IDX_T>;
+  const float4* u4 = reinterpret_cast<const float4*>(s_u);   // broadcast reads, four rows at a time
+  bool ok = true;
+  const auto count = [&](uint32_t key) {
+    const uint32_t bin = key >> 20;
+    atomicAdd(&s_hp[bin >> 1], (bin & 1u) ? 0x10000u : 1u);
+  };
+#pragma unroll 1
+  for (int ri = 0; ri < g.nrounds; ++ri) {
+    const int t = 2 * ri + g.half;
+    if (t < g.ntiles) {                                     // uniform over each half (four whole warps)
+      const int s = t % nring;
+      ok = mbar_wait(&full[s], (unsigned)((t / nring) & 1)) && ok;
+      const unsigned char* tile = ring + s * kTileBytes + g.pp * 4;
+      if (Geo::CPT == 2) {
+        float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int jq = 0; jq < kMaxR; jq += 4) {
+          const float4 uq = u4[jq / 4];
+          const float uj[4] = {uq.x, uq.y, uq.z, uq.w};
+#pragma unroll
+          for (int x = 0; x < 4; ++x) {
+            const uint32_t wv = *reinterpret_cast<const uint32_t*>(tile + (jq + x) * Geo::ROWB);
+            acc = __ffma2_rn(make_float2(uj[x], uj[x]), make_float2(__uint_as_float(wv << 16),
+                                                                     __uint_as_float(wv & 0xffff0000u)), acc);
+          }
+        }
+        const int c = g.a0 + t * Geo::TW + 2 * g.pp;
+        const bool in0 = c >= g.c0 && c < g.c1, in1 = c + 1 >= g.c0 && c + 1 < g.c1;
+        const uint32_t k0 = in0 ? score_key(acc.x) : 0u, k1 = in1 ? score_key(acc.y) : 0u;
+        if (in0) { count(k0); if (so) so[c] = acc.x; }
+        if (in1) { count(k1); if (so) so[c + 1] = acc.y; }
+        tmem_st2(g.tlane + 2u * ri, k0, k1);
+      } else {
+        float acc = 0.f;
+#pragma unroll
+        for (int jq = 0; jq < kMaxR; jq += 4) {
+          const float4 uq = u4[jq / 4];
+          const float uj[4] = {uq.x, uq.y, uq.z, uq.w};
+#pragma unroll
+          for (int x = 0; x < 4; ++x)
+            acc = fmaf(uj[x], __uint_as_float(*reinterpret_cast<const uint32_t*>(tile + (jq + x) * Geo::ROWB)), acc);
+        }
+        const int c = g.a0 + t * Geo::TW + g.pp;
+        const bool in0 = c >= g.c0 && c < g.c1;
+        const uint32_t k0 = in0 ? score_key(acc) : 0u;
+        if (in0) { count(k0); if (so) so[c] = acc; }
+        tmem_st1(g.tlane + (uint32_t)ri, k0);
+      }
+    } else {                                                // no tile for this half in the last round: keys 0
+      if (Geo::CPT == 2) tmem_st2(g.tlane + 2u * ri, 0u, 0u);
+      else tmem_st1(g.tlane + (uint32_t)ri, 0u);
+    }
+    half_sync(g.half);                                      // this half's tile t is consumed
+    if (g.pp == 0 && t + nring < g.ntiles) tkey_issue(g, map, ring, full, nring, seg_row, t + nring);
+  }
+  return ok;
+}
 
 // `pre` runs once, after the first two batches of loads are in flight and before u is first read (the fused kernel
 // computes u there, so its latency hides under the loads); it must be called by every thread of the CTA.
@@ -551,8 +739,11 @@ __device__ void pivot_round(cg::cluster_group& cluster, int CS, int crank, const
 }
 
 template <typename KV_T, typename IDX_T, int HP>
-__global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodeParams p,
+                                                                   const __grid_constant__ CUtensorMap zmap) {
   unsigned char* dsm = g_dsm;
+  __shared__ __align__(8) uint64_t s_full[kMaxRing];
+  __shared__ uint32_t s_taddr;
   __shared__ __align__(16) float s_u[kMaxR];
   __shared__ float s_pre[kWarps * 32];
   __shared__ int s_sltot[kMaxCluster];
@@ -588,11 +779,29 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   const int kb = (c0 / 32) * 32;                        // bitmap bit i and list column i stand for column kb + i
 
   // ---------------- prologue: z column (rank 0 of the cluster) and u ----------------
+  // resident-key scan: the ring's barriers and 256 TMEM columns, then the first tiles go in flight before u is known
+  const bool tkl = p.tkeys && p.select_mode == 1 && p.scan;   // launch-uniform: decides cluster-wide control flow
+  const bool tk = tkl && nloc > 0;                              // this CTA holds keys in TMEM
+  if (tk) {
+    if (tid == 0) {
+      for (int i = 0; i < p.nring; ++i) mbar_init(&s_full[i], 1);
+      mbar_init_fence();
+    }
+    if (tid < 32) { tmem_alloc(&s_taddr, kTmemCols); tmem_relinquish(); }
+  }
   if (p.select_mode == 1) {
-    for (int i = tid; i < 4096; i += kThreads) s_hist[i] = 0u;
-    for (int i = tid; i < 2 * p.nwp; i += kThreads) s_gt[i] = 0u;   // s_eq follows s_gt
+    for (int i = tid; i < (tk ? 2048 : 4096); i += kThreads) s_hist[i] = 0u;   // tk: the packed scan histogram
+    if (!tk) for (int i = tid; i < 2 * p.nwp; i += kThreads) s_gt[i] = 0u;   // s_eq follows s_gt (tk: after the scan)
     if (tid == 0) { g_list_count = 0u; g_list_thr = 0u; }
   }
+  if (tk) {
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
+  }
+  const TKeyGeo<IDX_T> tg(c0, c1, tk ? s_taddr : 0u);
+  if (tk && tid == 0)
+    for (int t = 0; t < p.nring && t < tg.ntiles; ++t) tkey_issue(tg, &zmap, dsm + p.ring_off, s_full, p.nring, seg * p.r, t);
   if (p.k_new && crank == 0) write_z_column<IDX_T>(p, b, g);
   // selection-independent inputs of the compaction, loaded while the scan's first loads are in flight (at once when
   // this CTA scans nothing): the segment's first candidate row, this CTA's share of F into the attend list, and
@@ -627,13 +836,34 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   // u is computed inside the scan, under its first loads (compute_u ends with the __syncthreads() that also
   // publishes the cleared histogram before any key is counted); a CTA without columns needs no u
   const auto pre_u = [&]() { load_rows([&]() { compute_u<IDX_T>(p, b, g, s_u, s_pre); }); };
-  const bool scans = p.scan && nloc > 0;
-  if (!scans) load_rows([]() {});
+  const bool scans = p.scan && nloc > 0 && !tk;
+  if (!scans && !tk) load_rows([]() {});
 
   // ---------------- scan: candidate scores -> order keys ----------------
   float* so = p.scores_out ? p.scores_out + (size_t)seg * p.M - p.lo : nullptr;   // indexed by column
   const ZSrc zsrc{reinterpret_cast<const IDX_T*>(p.zT) + (size_t)seg * p.r * p.C, p.r, p.C, p.zvec};
-  if (scans) {
+  if (tk) {
+    pre_u();                                               // ends with __syncthreads(): u and the cleared histogram
+    if (!tkey_scan<IDX_T>(tg, &zmap, dsm + p.ring_off, s_full, p.nring, seg * p.r, s_u, s_hist, so))
+      atomicOr(p.err, kErrWaitLimit);
+    tmem_wait_st();
+    tmem_fence_before_sync();
+    __syncthreads();
+    tmem_fence_after_sync();
+    // unpack the 16-bit bin pairs into the 4096-word histogram (over the packed words and the ring's first stage,
+    // both free now), and clear the bitmaps, which reuse the ring too
+    uint32_t hp[2048 / kThreads];
+#pragma unroll
+    for (int i = 0; i < 2048 / kThreads; ++i) hp[i] = s_hist[tid + i * kThreads];
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2048 / kThreads; ++i) {
+      const int wi = tid + i * kThreads;
+      s_hist[2 * wi] = hp[i] & 0xffffu;
+      s_hist[2 * wi + 1] = hp[i] >> 16;
+    }
+    for (int i = tid; i < 2 * p.nwp; i += kThreads) s_gt[i] = 0u;
+  } else if (scans) {
     if (p.select_mode == 1) {
       if (so) {
         SinkFirst<true> sk{so, p.list_off, p.cap, p.k, kb};
@@ -662,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
   uint32_t tau = 0;
   int k_rem = 0;
   bool selected = false;
-  if (p.select_mode == 1 && CS == 1 && g_list_count <= (unsigned)p.cap) {
+  if (p.select_mode == 1 && CS == 1 && (tkl || g_list_count <= (unsigned)p.cap)) {
     // One CTA, list complete: one warp finds the pivot bin from the histogram; if that bin holds at most kSmall
     // keys, one list pass marks every key above it and gathers the bin's keys, and two radix passes over the
     // gathered keys alone find the exact k-th key.
@@ -674,13 +904,47 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
     }
     __syncthreads();
     const int b0 = s_piv[0], gt0 = s_piv[1], n0 = s_piv[2];
-    if (n0 <= kSmall) {
+    // resident keys: compact every key of bin >= b0 (about k + n0 of them) into the candidate list -- a count
+    // sweep, a block scan for each warp's first slot, a write sweep whose slots come from warp votes (warp-uniform
+    // branches only) -- so the list path below runs on it; if the list region cannot hold them, the general path
+    // re-reads the keys from TMEM instead
+    bool have = n0 <= kSmall;
+    int n_list = tkl ? 0 : (int)g_list_count;
+    if (tk && have) {
+      int nge = 0;
+      tg.for_each_chunk([&](const uint32_t (&r)[8], int) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nge += (int)((int)(r[e] >> 20) >= b0);
+      });
+      int tot;
+      const int incl = block_inclusive_scan(nge, s_ws, &tot);
+      have = tot <= p.cap;                               // CTA-uniform
+      if (have) {
+        uint32_t* lk = reinterpret_cast<uint32_t*>(dsm + p.list_off);
+        uint32_t* lc = lk + p.cap;
+        const unsigned lt = (1u << (tid & 31)) - 1u;
+        int base = __shfl_sync(0xffffffffu, incl - nge, 0);   // the warp's first slot (threads are warp-major)
+        tg.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const bool m = (int)(r[e] >> 20) >= b0;
+            const unsigned bal = __ballot_sync(0xffffffffu, m);
+            if (bal) {
+              const int o = base + __popc(bal & lt);
+              if (m) { lk[o] = r[e]; lc[o] = (uint32_t)(tg.col(i0 + e) - kb); }
+              base += __popc(bal);
+            }
+          }
+        });
+        n_list = tot;
+      }
+    }
+    if (have) {
       uint32_t* skey = s_hist;                           // [kSmall] keys of bin b0, then [kSmall] their columns
       uint32_t* scol = s_hist + kSmall;
       unsigned* whist = s_hist + 2 * kSmall;             // [1024] digit histogram of the gathered keys
       if (tid == 0) g_list_thr = 0u;                     // reused as the gathered keys' fill counter
       __syncthreads();
-      const int n_list = (int)g_list_count;
       const unsigned lt = (1u << (tid & 31)) - 1u;
       constexpr int U = 4;                               // list entries per thread and step, loads batched
       for (int base = 0; base < n_list; base += U * kThreads) {   // uniform trip count: warp-aggregated appends
@@ -755,7 +1019,9 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
     pivot_round(cluster, CS, crank, s_hist, s_slice, s_sltot, s_piv, s_ws, 4096, p.k, b0, gt0);
     const unsigned cnt = g_list_count;
     bool use_list;
-    if (CS > 1) {
+    if (tkl) {
+      use_list = false;                                  // every CTA's keys are in its TMEM
+    } else if (CS > 1) {
       if (tid < CS) cluster.map_shared_rank(s_cflag, tid)[crank] = cnt > (unsigned)p.cap ? 1 : 0;
       cluster.sync();
       use_list = true;
@@ -774,7 +1040,16 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
         for (int i = tid; i < 1024; i += kThreads) s_hist[i] = 0u;
         __syncthreads();
       }
-      if (use_list) {
+      if (tkl) {
+        if (tk && pass < 2)
+          tg.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e)                  // prefix >= 7 << 20: key 0 (no candidate) never matches
+              if ((r[e] & pmask) == prefix) atomicAdd(&s_hist[(r[e] >> shift) & 1023u], 1u);
+          });
+        else if (tk)
+          tkey_marks(tg, prefix, s_gt, s_eq, p.nwp, s_skey);
+      } else if (use_list) {
         for (int i = tid; i < n_list; i += kThreads) {
           const uint32_t key = s_lkey[i];
           if (pass < 2) {
@@ -800,6 +1075,12 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
     }
     tau = prefix;
     __syncthreads();
+  }
+
+  if (tk) {                                              // every key has been read back: release the TMEM
+    tmem_fence_before_sync();
+    __syncthreads();
+    if (tid < 32) tmem_dealloc(s_taddr, kTmemCols);
   }
 
   // ---------------- ordered selection: chosen candidates in ascending position order ----------------

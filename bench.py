@@ -90,7 +90,7 @@ def ledger(B, G, h, L, rho, layers, zb, eb):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region (every 100 ms)."""
+    """nvidia-smi clock / throttle sampling during the timed region (every 20 ms)."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -102,7 +102,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -151,63 +151,124 @@ def measured_peak():
 
 
 # ------------------------------------------------------------------------------------------------ CPU side
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+class CpuReferencePath:
+    """The reference's hot path on the host cores: oracle/torch_ref.py, the reference's own torch operators
+    (decode.py:145-163 and the K/V copies of qwen_wrap.py:90-106) in its dtypes (bf16 K/V, the index dtype for z),
+    over the workload's B requests at legal length L. Host memory holds one layer's caches ([B,G,L,d] K and V, [B,G,r,L]
+    index), which every layer of the step reuses with its own indexer weights and step inputs. Caches are filled from
+    one N(0,1) block (each request and tensor at its own offset), so building them costs a copy, not a random draw."""
+
+    def __init__(self, B, G, h, L, rho, layers, zb):
+        import torch
+        from attention_lab_b200.selection import build_step_plan, fixed_budget
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.torch, self.B, self.G, self.h, self.L, self.layers = torch, B, G, h, L, layers
+        bf = torch.bfloat16
+        idt = bf if zb == 2 else torch.float32
+        gen = torch.Generator().manual_seed(0)
+        block = torch.randn(1 << 24, generator=gen).to(bf)
+        n_blk = block.numel()
+
+        def filled(shape, dtype, scale, salt):
+            t = torch.empty(shape, dtype=dtype)
+            flat = t.view(-1)
+            step = 7919 * (salt + 1)
+            for i, a in enumerate(range(0, flat.numel(), n_blk)):
+                n = min(n_blk, flat.numel() - a)
+                off = (i * step) % (n_blk - n + 1) if n < n_blk else 0
+                flat[a:a + n].copy_(block[off:off + n])
+            if scale != 1.0:
+                t.mul_(scale)
+            return t
+        C = L
+        self.K = filled((B, G, C, D), bf, 1.0, 1)
+        self.V = filled((B, G, C, D), bf, 1.0, 2)
+        self.Z = filled((B, G, R, C), idt, 0.23, 3)
+        self.WQ = [(torch.randn(G, h * D, R, generator=gen) * (0.02 / math.sqrt(R))).to(idt) for _ in range(layers)]
+        self.WK = [(torch.randn(G, R, D, generator=gen) * 0.02).to(idt) for _ in range(layers)]
+        self.Q = [torch.randn(B, G, h, 1, D, generator=gen).to(bf) for _ in range(layers)]
+        self.QP = [torch.randn(B, G, h, 1, D, generator=gen).to(idt) for _ in range(layers)]
+        self.KPN = [torch.randn(B, G, 1, D, generator=gen).to(idt) for _ in range(layers)]
+        self.KN = [torch.randn(B, G, 1, D, generator=gen).to(bf) for _ in range(layers)]
+        self.plan = build_step_plan(B, G, C, L, fixed_budget(L, rho), "cpu")
+
+    def layer(self, l):
+        from oracle import torch_ref as tr
+        p = self.plan
+        with self.torch.inference_mode():
+            tr.append_kv(self.K, self.V, self.L - 1, self.KN[l], self.KN[l])
+            out, _ = tr.sparse_decode_step_kernel(self.Q[l], self.QP[l], self.K, self.V, self.Z, self.WQ[l], self.WK[l],
+                                                  p.fixed_rows, p.off_lo, p.lo, p.hi, p.k, p.selected_count,
+                                                  k_pre_new=self.KPN[l], write_col=p.write_col, scale=1 / math.sqrt(D))
+        return out
+
+    def step(self):
+        for l in range(self.layers):
+            self.layer(l)
+
+    def describe(self):
+        return (f"oracle/torch_ref.py: the reference's torch operators (matmul, topk, cat, index_select, SDPA, copy_) "
+                f"in bf16, B={self.B} requests x {self.layers} layers at L={self.L} per step, "
+                f"{self.threads} torch threads on {cpu_model()}")
+
+
 def cpu_sample(args, B, G, h, L, rho, layers, budget_s):
-    """Time the CPU restatement of the reference's step (oracle.cpu_sparse_request, float32 numpy) on a bounded
-    sample: P requests of one layer in parallel (one per worker thread), repeated until ~budget_s of wall time.
-    Returns tokens/s of the full workload (B requests x layers layers) extrapolated from the per-request cost."""
-    import numpy as np
-    from concurrent.futures import ThreadPoolExecutor
-    from threadpoolctl import threadpool_limits
-    from oracle import oracle as orc
-    lg = ledger(B, G, h, L, rho, layers, 2, 2)
-    workers = max(1, min(64, os.cpu_count() or 1))
-    rng = np.random.default_rng(0)
-    C = L
-    K = rng.standard_normal((G, C, D), dtype=np.float32)
-    V = rng.standard_normal((G, C, D), dtype=np.float32)
-    zT = rng.standard_normal((G, R, C), dtype=np.float32)
-    wq = (rng.standard_normal((G, h * D, R), dtype=np.float32) * 0.02)
-    wk = (rng.standard_normal((G, R, D), dtype=np.float32) * 0.02)
-    reqs = [(rng.standard_normal((G, h, D), dtype=np.float32), rng.standard_normal((G, h, D), dtype=np.float32),
-             rng.standard_normal((G, D), dtype=np.float32)) for _ in range(workers)]
-    zTs = [zT.copy() for _ in range(workers)]
-
-    def one(i):
-        q, qp, kn = reqs[i]
-        return orc.cpu_sparse_request(q, qp, K, V, zTs[i], wq, wk, kn, lg["lo"], lg["hi"], lg["k"], L, 1 / math.sqrt(D))
-
-    with threadpool_limits(1), ThreadPoolExecutor(workers) as ex:
-        list(ex.map(one, range(workers)))                       # warm-up
-        rounds, t0 = 0, time.perf_counter()
-        while True:
-            list(ex.map(one, range(workers)))
-            rounds += 1
-            if time.perf_counter() - t0 >= budget_s:
-                break
-        wall = time.perf_counter() - t0
-    per_round = wall / rounds                                   # `workers` requests of one layer
-    step_s = per_round * (B / workers) * layers                 # B requests x all layers
-    return {"value": B / step_s, "unit": "tokens/s", "cores": workers, "kind": "port",
-            "sample": f"{rounds} rounds x {workers} concurrent (layer, request) steps of the workload's shape "
-                      f"(L={L}, k={lg['k']}, float32 numpy, one thread each), {wall:.1f} s wall; "
-                      f"tokens/s = B / (layers x B/workers x round time)",
-            "ms_per_layer_request": per_round * 1e3}
+    """The cpu_baseline of the GPU arm: layers of the step through CpuReferencePath until ~budget_s has passed
+    (at least one), tokens/s = B / (layers x mean layer time). Returns the cpu_baseline object."""
+    ref = CpuReferencePath(B, G, h, L, rho, layers, 2 if args.index_dtype == "bf16" else 4)
+    ref.layer(0)                                                  # warm-up
+    n, t0 = 0, time.perf_counter()
+    while True:
+        ref.layer(n % layers)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    per_layer = (time.perf_counter() - t0) / n
+    return {"value": B / (per_layer * layers), "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+            "cpu_model": cpu_model(),
+            "sample": f"{n} layer(s) of the step ({ref.describe()}); tokens/s = B / (layers x mean layer time)"}
 
 
 def run_reference_arm(args):
+    """The reference arm: W warm-up and K timed FULL steps (every layer, every request) of the reference's path on
+    the host cores (CpuReferencePath), timed with the wall clock; rank 0 only (other ranks exit at once)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     layers, B, G, h, L, rho, desc = workload(args)
-    budget = max(2.0, min(args.cpu_seconds, 60.0))
-    cpu = cpu_sample(args, B, G, h, L, rho, layers, budget)
-    line = {"impl": "reference", "metric": metric_name(args.workload), "value": cpu["value"], "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1e3 * B / cpu["value"], "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic",
+    zb = 2 if args.index_dtype == "bf16" else 4
+    ref = CpuReferencePath(B, G, h, L, rho, layers, zb)
+    for _ in range(args.warmup):
+        ref.step()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        ref.step()
+        times.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(times)
+    value = B / (ms / 1e3)
+    sample = f"{args.steps} full step(s) after {args.warmup} warm-up step(s): {ref.describe()}"
+    line = {"impl": "reference", "metric": metric_name(args.workload), "value": round(value, 3), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_of(args, desc, B, G, h, L, rho, layers),
-            "cpu_baseline": {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": cpu["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": ref.threads, "kind": "port",
+                             "cpu_model": cpu_model(), "sample": sample},
+            "timed_s": round(sum(times), 2),
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -538,32 +599,46 @@ def main():
     t_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
     value = world * B / (t_ms / 1e3)
 
-    # ---- roofline of the dominant kernel: each fused launch timed on its own stream with events
-    n_roof = min(args.steps, 10)
-    starts = [[torch.cuda.Event(enable_timing=True) for _ in range(layers)] for _ in range(n_roof)]
-    ends = [[torch.cuda.Event(enable_timing=True) for _ in range(layers)] for _ in range(n_roof)]
+    # ---- roofline of the dominant kernel: the `layers` fused launches of one step captured alone as a CUDA graph and
+    #      replayed (launch_ms = graph time / layers, no per-launch event overhead); each launch also timed on its own
+    #      with events as a cross-check; the appends timed alone
+    fgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(fgraph, stream=stream):
+        for l in range(layers):
+            _lib.check(lib.al_sparse_decode_step(*S_ARGS[l]))
+    n_roof = max(3, min(args.steps, 10))
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(layers)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(layers)]
     a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
+        fgraph.replay()
+        g0.record(stream)
         for i in range(n_roof):
-            for l in range(layers):
-                starts[i][l].record(stream)
-                _lib.check(lib.al_sparse_decode_step(*S_ARGS[l]))
-                ends[i][l].record(stream)
+            fgraph.replay()
+        g1.record(stream)
+        for l in range(layers):
+            starts[l].record(stream)
+            _lib.check(lib.al_sparse_decode_step(*S_ARGS[l]))
+            ends[l].record(stream)
         a0.record(stream)
         for i in range(n_roof):
             for l in range(layers):
                 _lib.check(lib.al_append_kvz(*A_ARGS[l]))
         a1.record(stream)
     torch.cuda.synchronize(dev)
-    durs = [starts[i][l].elapsed_time(ends[i][l]) for i in range(n_roof) for l in range(layers)]
-    fused_ms = max_over_ranks(statistics.mean(durs))
+    fused_ms = max_over_ranks(g0.elapsed_time(g1) / (n_roof * layers))
+    event_ms = statistics.mean(starts[l].elapsed_time(ends[l]) for l in range(layers))
     append_ms = a0.elapsed_time(a1) / (n_roof * layers)
+    del fgraph
     peak, peak_src = measured_peak()
     achieved = lg["per_launch"] / (fused_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "traffic": None,
                 "kernel": "sparse_step_kernel (fused z column + u + scan + radix top-k + gather-free attend)",
-                "bytes_per_launch": lg["per_launch"], "launch_ms": round(fused_ms, 5), "peak_source": peak_src,
+                "bytes_per_launch": lg["per_launch"], "launch_ms": round(fused_ms, 5),
+                "launch_timing": f"CUDA graph of the {layers} fused launches of a step, {n_roof} replays, time / launches",
+                "launch_ms_events": round(event_ms, 5), "peak_source": peak_src,
                 "bytes_rule": "B x (G*r*M*zb + S*G*d*2*eb) per launch (scripts/roofline.py:61-74 terms)"}
     traffic_file = ROOT / "profiles" / f"traffic_{args.workload}_{args.index_dtype}.json"
     if traffic_file.exists():
@@ -573,27 +648,48 @@ def main():
             pass
 
     # ---- e2e through the public API with host buffers: H2D of every layer's step inputs, the drop-in operators,
-    #      D2H of every layer's attention output
+    #      D2H of every layer's attention output. The copies run on two side streams so that layer l's inputs land
+    #      while earlier layers compute and each output leaves as soon as it is written; inputs are double-buffered
+    #      across steps. The timed region ends after the last D2H copy.
     e2e = None
     if not args.no_e2e:
         host_in = [[t.cpu().pin_memory() for t in (Q[l], QP[l], KPN[l], KN[l], VN[l])] for l in range(layers)]
         host_out = [torch.empty(OUT[0].shape, dtype=kvt).pin_memory() for _ in range(layers)]
-        dev_in = [[torch.empty_like(t) for t in (Q[l], QP[l], KPN[l], KN[l], VN[l])] for l in range(layers)]
+        dev_in = [[[torch.empty_like(t) for t in (Q[l], QP[l], KPN[l], KN[l], VN[l])] for l in range(layers)]
+                  for _ in range(2)]
         h2d = sum(t.numel() * t.element_size() for row in host_in for t in row)
         d2h = sum(t.numel() * t.element_size() for t in host_out)
+        h2d_s, d2h_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        ev_in = [[torch.cuda.Event() for _ in range(layers)] for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(layers)]
+        done = [torch.cuda.Event(), torch.cuda.Event()]
+        state = {"i": 0}
 
         def e2e_step():
+            j = state["i"] % 2
+            first = state["i"] < 2
+            state["i"] += 1
+            with torch.cuda.stream(h2d_s):
+                if not first:
+                    h2d_s.wait_event(done[j])            # the step that last used these buffers has consumed them
+                for l in range(layers):
+                    for dst, src in zip(dev_in[j][l], host_in[l]):
+                        dst.copy_(src, non_blocking=True)
+                    ev_in[j][l].record(h2d_s)
             for l in range(layers):
-                for dst, src in zip(dev_in[l], host_in[l]):
-                    dst.copy_(src, non_blocking=True)
-            for l in range(layers):
-                q, qp, kpn, kn, vn = dev_in[l]
+                stream.wait_event(ev_in[j][l])
+                q, qp, kpn, kn, vn = dev_in[j][l]
                 al.append_kvz(Ks[l], Vs[l], None, L - 1, kn, vn)
                 out = al.sparse_decode_step_kernel(q, qp, Ks[l], Vs[l], Zs[l], WQ[l], WK[l], plan.fixed_rows,
                                                    plan.off_lo, plan.lo, plan.hi, plan.k, plan.selected_count,
                                                    k_pre_new=kpn, write_col=plan.write_col, scale=scale,
                                                    cluster=args.cluster)
-                host_out[l].copy_(out, non_blocking=True)
+                ev_out[l].record(stream)
+                with torch.cuda.stream(d2h_s):
+                    d2h_s.wait_event(ev_out[l])
+                    host_out[l].copy_(out, non_blocking=True)
+                    out.record_stream(d2h_s)
+            done[j].record(stream)
 
         n_e2e = max(3, min(args.steps, 30))
         with torch.cuda.stream(stream):
@@ -606,23 +702,25 @@ def main():
             f0.record(stream)
             for _ in range(n_e2e):
                 e2e_step()
+            stream.wait_stream(d2h_s)                    # the last outputs are on the host
             f1.record(stream)
         torch.cuda.synchronize(dev)
         barrier()
         e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / n_e2e
         e2e = {"value": world * B / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 4), "steps": n_e2e,
-               "path": "attention_lab_b200.append_kvz + sparse_decode_step_kernel per layer, pinned host I/O"}
+               "path": "attention_lab_b200.append_kvz + sparse_decode_step_kernel per layer, pinned host I/O on two "
+                       "copy streams overlapping the compute"}
 
     # ---- same-box baselines (rank 0 reports its own): dense decode over the same caches
     baselines = None
     if not args.no_baselines and rank == 0:
-        baselines = same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale)
+        baselines = same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale,
+                                       sparse_inputs=(Zs, WQ, WK, QP, KPN, plan))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_sample(args, B, G, h, L, rho, layers, args.cpu_seconds)
-        cpu = {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")}
 
     if rank == 0:
         line = {"metric": metric_name(args.workload), "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
@@ -640,9 +738,11 @@ def main():
     return 0
 
 
-def same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale):
-    """Dense decode over the same 36-layer caches: torch SDPA with the h heads folded into the query axis (the
-    reference's full_attention(backend="sdpa_fold"), full.py:31-34) and this library's own dense kernel."""
+def same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale, sparse_inputs=None):
+    """Same-box baselines over the same caches: dense decode with torch SDPA, the h heads folded into the query axis
+    (the reference's full_attention(backend="sdpa_fold"), full.py:31-34), this library's own dense kernel, and the
+    reference's own sparse path run by torch on the GPU -- the operators of decode.py:145-163 (z column copy, u matmul,
+    candidate matmul, torch.topk, cat with F, two index_selects, SDPA; decode.py:86-93,131-142, indexer.py:15-29)."""
     import torch.nn.functional as F
     out = {}
 
@@ -675,6 +775,27 @@ def same_box_baselines(torch, al, Ks, Vs, Q, L, layers, B, stream, scale):
         out["torch_sdpa_fold_dense"] = {"error": str(e)[:200]}
     ms = timed(ours_dense)
     out["ours_dense"] = {"tokens_per_s": round(B / (ms / 1e3), 2), "ms_per_step": round(ms, 3)}
+    if sparse_inputs is not None:
+        Zs, WQ, WK, QP, KPN, plan = sparse_inputs
+
+        def torch_reference_sparse():
+            for l in range(layers):
+                q, zT = Q[l], Zs[l]
+                b, g, h, _, d = q.shape
+                wc = plan.write_col
+                zT[..., wc:wc + 1].copy_(torch.matmul(WK[l].unsqueeze(0), KPN[l].transpose(-1, -2)))
+                u = torch.matmul(QP[l].permute(0, 1, 3, 2, 4).reshape(b, g, 1, h * d), WQ[l].unsqueeze(0))
+                top = torch.topk(torch.matmul(u, zT[..., plan.lo:plan.hi]), plan.k, dim=-1).indices.view(b, g, plan.k)
+                rows = torch.cat([plan.fixed_rows, top + plan.off_lo], dim=-1).view(-1)
+                S = plan.selected_count
+                k_sub = Ks[l].view(-1, d).index_select(0, rows).view(b, g, S, d)
+                v_sub = Vs[l].view(-1, d).index_select(0, rows).view(b, g, S, d)
+                F.scaled_dot_product_attention(q.reshape(b, g, h, d), k_sub, v_sub, scale=scale)
+        try:
+            ms = timed(torch_reference_sparse)
+            out["torch_reference_sparse_path"] = {"tokens_per_s": round(B / (ms / 1e3), 2), "ms_per_step": round(ms, 3)}
+        except RuntimeError as e:
+            out["torch_reference_sparse_path"] = {"error": str(e)[:200]}
     return out
 
 

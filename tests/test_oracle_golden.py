@@ -183,3 +183,23 @@ def test_selectors_b_and_c_known_answers():
     assert np.array_equal(a, b) and len(set(a[6:].tolist())) == 7 and all(4 <= r < 90 for r in a[6:])
     with pytest.raises(ValueError):
         orc.select_rows_recent(fixed, off_lo, 4, 90, 87)
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_torch_restatement_reproduces_the_reference(name):
+    """oracle/torch_ref.py (the reference arm of bench.py) runs the reference's own torch operators in the reference's
+    dtypes: on the golden inputs it must give the reference's rows, z column and output."""
+    from oracle import torch_ref as tr
+    case, g = cs.CASES[name], load(name)
+    t = cs.build(case)
+    c = cs.step_constants(case)
+    zT = t["zT"].clone()
+    with torch.inference_mode():
+        out, rows = tr.sparse_decode_step_kernel(t["q"], t["q_pre"], t["k"], t["v"], zT, t["wq_t"], t["wk"],
+                                                 torch.from_numpy(c["fixed_rows"]), torch.from_numpy(c["off_lo"]),
+                                                 c["lo"], c["hi"], c["k"], c["S"], k_pre_new=t["k_pre_new"],
+                                                 write_col=c["write_col"], scale=1 / math.sqrt(case.d),
+                                                 canonical_order=case.canonical)
+    assert np.array_equal(zT[..., c["write_col"]].to(torch.float32).numpy(), g["zcol"])
+    assert np.array_equal(rows.numpy(), g["rows"])
+    assert np.abs(out.to(torch.float32).numpy() - g["out"]).max() <= 1e-6
