@@ -224,6 +224,8 @@ struct TKeyGeo {
   }
   // column of key i of this thread
   __device__ __forceinline__ int col(int i) const { return a0 + (2 * (i / CPT) + half) * TW + CPT * pp + i % CPT; }
+  // col(i0 + e) - col(i0) for a chunk start i0 (a multiple of 8)
+  static __device__ __forceinline__ int colstep(int e) { return (e / CPT) * 2 * TW + e % CPT; }
   // f(keys[8], i0) for each chunk of 8 of this thread's keys (key i0 + e in keys[e]; entries past the thread's keys
   // read as 0, like a column outside the candidates); every thread of the CTA calls it (warp-collective loads)
   template <typename F>
@@ -240,58 +242,6 @@ struct TKeyGeo {
     }
   }
 };
-
-// Spread the low 16 bits of x to the even bit positions.
-__device__ __forceinline__ uint32_t spread16(uint32_t x) {
-  x &= 0xffffu;
-  x = (x | (x << 8)) & 0x00ff00ffu;
-  x = (x | (x << 4)) & 0x0f0f0f0fu;
-  x = (x | (x << 2)) & 0x33333333u;
-  return (x | (x << 1)) & 0x55555555u;
-}
-
-// The selection marks from the keys in TMEM: bit (column - a0) of gt / eq for key > tau / key == tau. A warp's keys of
-// one round cover whole bitmap words (a0 is a multiple of 32): 32 consecutive columns (fp32 index) or 64 columns
-// (bf16: the even and odd columns of 32 lanes, interleaved), so each word is built from warp votes and written once
-// with a plain store -- no atomics, no divergence. Words at or beyond nwp are not written (their columns lie past
-// the CTA's candidates). Keys of chosen columns also go to skey[column - a0] when skey is given.
-template <typename IDX_T>
-__device__ void tkey_marks(const TKeyGeo<IDX_T>& g, uint32_t tau, uint32_t* gt, uint32_t* eq, int nwp,
-                           uint32_t* skey) {
-  using Geo = TKeyGeo<IDX_T>;
-  const int lane = threadIdx.x & 31, wq = (threadIdx.x >> 5) & 3;
-  g.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
-    if (Geo::CPT == 2) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int t = 2 * (i0 / 2 + j) + g.half;
-        const uint32_t g0 = __ballot_sync(0xffffffffu, r[2 * j] > tau);
-        const uint32_t g1 = __ballot_sync(0xffffffffu, r[2 * j + 1] > tau);
-        const uint32_t e0 = __ballot_sync(0xffffffffu, r[2 * j] == tau);
-        const uint32_t e1 = __ballot_sync(0xffffffffu, r[2 * j + 1] == tau);
-        const int wi = 8 * t + 2 * wq + (lane >> 4), sh = lane & 16;
-        if ((lane & 15) == 0 && t < g.ntiles && wi < nwp) {
-          gt[wi] = spread16(g0 >> sh) | (spread16(g1 >> sh) << 1);
-          eq[wi] = spread16(e0 >> sh) | (spread16(e1 >> sh) << 1);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int t = 2 * (i0 + e) + g.half;
-        const uint32_t gw = __ballot_sync(0xffffffffu, r[e] > tau);
-        const uint32_t ew = __ballot_sync(0xffffffffu, r[e] == tau);
-        const int wi = 4 * t + wq;
-        if (lane == 0 && t < g.ntiles && wi < nwp) { gt[wi] = gw; eq[wi] = ew; }
-      }
-    }
-    if (skey) {
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (r[e] >= tau) skey[g.col(i0 + e) - g.a0] = r[e];
-    }
-  });
-}
 
 // Issue tile t of the CTA's columns into ring stage t % nring.
 template <typename IDX_T>
@@ -314,7 +264,7 @@ __device__ __forceinline__ void half_sync(int half) {
 // and its leader thread re-arms a stage as soon as the half's 128 threads have read it. Returns false if a bounded
 // wait gave up.
 template <typename IDX_T>
-__device__ __noinline__ bool tkey_scan(const TKeyGeo<IDX_T>& g, const void* map, unsigned char* ring, uint64_t* full, int nring,
+__device__ __noinline__ bool tkey_scan(const TKeyGeo<IDX_T> g, const void* map, unsigned char* ring, uint64_t* full, int nring,
                           int seg_row, const float* s_u, unsigned* s_hp, float* so) {
   using Geo = TKeyGeo<IDX_T>;
   const float4* u4 = reinterpret_cast<const float4*>(s_u);   // broadcast reads, four rows at a time
@@ -922,18 +872,27 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
       if (have) {
         uint32_t* lk = reinterpret_cast<uint32_t*>(dsm + p.list_off);
         uint32_t* lc = lk + p.cap;
-        const unsigned lt = (1u << (tid & 31)) - 1u;
+        const int lane = tid & 31;
         int base = __shfl_sync(0xffffffffu, incl - nge, 0);   // the warp's first slot (threads are warp-major)
         tg.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
+          // one warp scan per chunk of 8 keys: this lane's matches go to consecutive slots after the lower lanes'
+          unsigned m = 0u;
 #pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const bool m = (int)(r[e] >> 20) >= b0;
-            const unsigned bal = __ballot_sync(0xffffffffu, m);
-            if (bal) {
-              const int o = base + __popc(bal & lt);
-              if (m) { lk[o] = r[e]; lc[o] = (uint32_t)(tg.col(i0 + e) - kb); }
-              base += __popc(bal);
-            }
+          for (int e = 0; e < 8; ++e) m |= ((int)(r[e] >> 20) >= b0 ? 1u : 0u) << e;
+          const int c = __popc(m);
+          int x = c;
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+          }
+          int o = base + x - c;
+          base += __shfl_sync(0xffffffffu, x, 31);
+          if (m) {
+            const int cb = tg.col(i0) - kb;               // key i0 + e sits at column cb + colstep(e)
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if ((m >> e) & 1u) { lk[o] = r[e]; lc[o] = (uint32_t)(cb + tg.colstep(e)); ++o; }
           }
         });
         n_list = tot;
@@ -1041,14 +1000,20 @@ __global__ void __launch_bounds__(kThreads, 2) sparse_step_kernel(const DecodePa
         __syncthreads();
       }
       if (tkl) {
-        if (tk && pass < 2)
+        if (tk)
           tg.for_each_chunk([&](const uint32_t (&r)[8], int i0) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e)                  // prefix >= 7 << 20: key 0 (no candidate) never matches
-              if ((r[e] & pmask) == prefix) atomicAdd(&s_hist[(r[e] >> shift) & 1023u], 1u);
+            for (int e = 0; e < 8; ++e) {                // prefix >= 7 << 20: key 0 (no candidate) never matches
+              const uint32_t key = r[e];
+              if (pass < 2) {
+                if ((key & pmask) == prefix) atomicAdd(&s_hist[(key >> shift) & 1023u], 1u);
+              } else if (key >= prefix) {
+                const uint32_t c = (uint32_t)(tg.col(i0 + e) - kb);
+                atomicOr(key > prefix ? &s_gt[c >> 5] : &s_eq[c >> 5], 1u << (c & 31));
+                if (s_skey) s_skey[c] = key;
+              }
+            }
           });
-        else if (tk)
-          tkey_marks(tg, prefix, s_gt, s_eq, p.nwp, s_skey);
       } else if (use_list) {
         for (int i = tid; i < n_list; i += kThreads) {
           const uint32_t key = s_lkey[i];
