@@ -297,7 +297,7 @@ def prefill_attention(q5: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Te
     mask = legal.repeat(h, 1).view(1, 1, h * T, n)
     out = F.scaled_dot_product_attention(q5.reshape(B, G, h * T, d), k_cache[:, :, :n], v_cache[:, :, :n],
                                          attn_mask=mask, scale=scale)
-    return out.view(B, G, h, T, d)
+    return out.reshape(B, G, h, T, d)
 
 
 class LabAttention(nn.Module):
@@ -372,7 +372,7 @@ class LabAttention(nn.Module):
         else:   # prefill: every legal position is read whatever the chunk size; the index table is filled on the way
             cache.append(l, k_main, v, k_pre=k_pre if build_z else None, wk=idx.wk if build_z else None)
             out = prefill_attention(q5, cache.k[l], cache.v[l], L0, self.scaling)
-        attn = out.view(B, self.num_heads, T, d).transpose(1, 2).reshape(B, T, self.num_heads * d)
+        attn = out.reshape(B, self.num_heads, T, d).transpose(1, 2).reshape(B, T, self.num_heads * d)
         return inner.o_proj(attn), None
 
 
@@ -561,6 +561,15 @@ def qwen3_config(shape: str, **overrides):
     return cfg
 
 
+def _reset_rope(model, device) -> None:
+    """Recompute the rotary inverse frequencies in float32 (a dtype cast of the whole model must not round them)."""
+    rot = model.model.rotary_emb
+    inv, scaling = rot.compute_default_rope_parameters(rot.config, device)
+    rot.inv_freq = inv
+    rot.original_inv_freq = inv.clone()
+    rot.attention_scaling = scaling
+
+
 def random_qwen3(cfg, *, device, dtype=torch.bfloat16, seed: int = 0):
     """A randomly initialised Qwen3 built directly on the device: parameters allocated without initialisation
     (meta device), then drawn N(0, initializer_range^2) from a seeded device generator, norm weights 1 (the
@@ -577,15 +586,28 @@ def random_qwen3(cfg, *, device, dtype=torch.bfloat16, seed: int = 0):
                 p.fill_(1.0)
             else:
                 p.normal_(0.0, std, generator=gen)
-        for name, b in model.named_buffers():
-            if name.endswith("inv_freq"):
-                rot = model.model.rotary_emb
-                inv, scaling = rot.rope_init_fn(rot.config, device)
-                b.copy_(inv)
-                rot.original_inv_freq = inv
+    if cfg.tie_word_embeddings:
+        model.tie_weights()
+    _reset_rope(model, device)
     model.eval()
     for p in model.parameters():
         p.requires_grad_(False)
-    if cfg.tie_word_embeddings:
-        model.tie_weights()
+    return model
+
+
+def tiny_qwen3(*, seed: int = 0, layers: int = 2, hidden: int = 256, heads: int = 4, groups: int = 2,
+               head_dim: int = 128, intermediate: int = 512, vocab: int = 256, max_positions: int = 4096,
+               dtype=torch.float32, device="cpu"):
+    """A small randomly initialised Qwen3 with the real module code and this library's head_dim (128), built on the
+    CPU from torch.manual_seed(seed) (so the same weights come out wherever the same torch runs), then moved."""
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(vocab_size=vocab, hidden_size=hidden, intermediate_size=intermediate, num_hidden_layers=layers,
+                      num_attention_heads=heads, num_key_value_heads=groups, head_dim=head_dim,
+                      max_position_embeddings=max_positions, tie_word_embeddings=False, attn_implementation="sdpa")
+    torch.manual_seed(int(seed))
+    model = Qwen3ForCausalLM(cfg).to(dtype).eval()
+    _reset_rope(model, "cpu")
+    model = model.to(device)
+    for p in model.parameters():
+        p.requires_grad_(False)
     return model
