@@ -14,7 +14,7 @@ What runs where:
     sparse decode (D0)  al_sparse_decode_step: the newest key's z column, u, candidate scores, top-k, F merge and the
                         gather-free attention, one launch per layer
     selectors B / C     their row lists (selection rules of decode.py:94-127), then al_gathered_attend
-    full decode (A)     al_dense_decode over [0, legal length)
+    full decode (A)     al_dense_decode over [0, legal length) (or torch SDPA, decode_backend="sdpa_fold")
     prefill read        torch scaled_dot_product_attention over [0, L0 + T) with the legality mask (a dense,
                         compute-bound read outside the decode hot path; full.py:17-45 sdpa_fold semantics)
 
@@ -45,6 +45,9 @@ except ImportError as _e:  # pragma: no cover
 # applies its own legality rules).
 MASK_BYPASS = {"full_attention": None}
 SELECTORS = ("index", "recent", "uniform")   # D0 / B / C
+# full-mode decode read: this library's dense kernel, or torch SDPA with the heads folded (the reference's A path,
+# full.py:31-34), kept as the same-box dense baseline
+DECODE_BACKENDS = ("kernel", "sdpa_fold")
 
 
 # ---------------------------------------------------------------------------------------------------------------------
@@ -237,9 +240,13 @@ class LabState:
     (index = D0, recent = B, uniform = C) and the plan of the step in flight (qwen_wrap.py:189-240)."""
 
     def __init__(self, cache: LabCache, indexers=None, *, mode: str = "full", selector: str = "index",
-                 uniform_seed: int = 0, sparse_layers=None, cache_guard=None, canonical_order=False):
+                 uniform_seed: int = 0, sparse_layers=None, cache_guard=None, canonical_order=False,
+                 decode_backend: str = "kernel"):
         if mode not in ("full", "sparse"):
             raise ValueError("mode must be 'full' or 'sparse'")
+        if decode_backend not in DECODE_BACKENDS:
+            raise ValueError(f"decode_backend must be one of {DECODE_BACKENDS}")
+        self.decode_backend = decode_backend
         if selector not in SELECTORS:
             raise ValueError(f"selector must be one of {SELECTORS}")
         if mode == "sparse" and selector == "index" and (indexers is None or not cache.has_index):
@@ -368,7 +375,11 @@ class LabAttention(nn.Module):
                     st.last_rows[l] = rows
             else:
                 cache.append(l, k_main, v, k_pre=k_pre if build_z else None, wk=idx.wk if build_z else None)
-                out = ops.dense_decode_step(q5, cache.k[l], cache.v[l], L0 + 1, scale=self.scaling)
+                if st.decode_backend == "kernel":
+                    out = ops.dense_decode_step(q5, cache.k[l], cache.v[l], L0 + 1, scale=self.scaling)
+                else:
+                    out = F.scaled_dot_product_attention(q5.reshape(B, G, h, d), cache.k[l][:, :, :L0 + 1],
+                                                         cache.v[l][:, :, :L0 + 1], scale=self.scaling)
         else:   # prefill: every legal position is read whatever the chunk size; the index table is filled on the way
             cache.append(l, k_main, v, k_pre=k_pre if build_z else None, wk=idx.wk if build_z else None)
             out = prefill_attention(q5, cache.k[l], cache.v[l], L0, self.scaling)

@@ -62,6 +62,12 @@ def parse():
     ap.add_argument("--context-split", action="store_true",
                     help="C4 measurement: one sequence split over the torchrun ranks (attention_lab_b200.context_split)")
     ap.add_argument("--no-graph", action="store_true", help="context split: launch every step from the host")
+    ap.add_argument("--model", choices=["c2", "c3"], default=None,
+                    help="end-to-end decode of a random-init Qwen3 through attention_lab_b200.runner: c2 (0.6B, 8192-token "
+                         "prompt, 256 greedy steps) or c3 (8B shape, 32K context per request); sparse vs dense")
+    ap.add_argument("--model-steps", type=int, default=0, help="decode steps of --model (0 = the config's)")
+    ap.add_argument("--model-graph", action="store_true",
+                    help="--model: also time one decode step captured as a CUDA graph and replayed at a fixed context")
     ap.add_argument("--prefill", action="store_true",
                     help="C5 measurement: the batched prefill scorer over one 8192-token chunk (8 heads, k=256)")
     return ap.parse_args()
@@ -361,6 +367,145 @@ def run_context_split(args):
         dist.destroy_process_group()
 
 
+def run_model(args):
+    """End-to-end greedy decode of a random-init Qwen3 through attention_lab_b200.runner (the reference wrapper's
+    interface on this library's kernels), sparse (rho = 1/32, index selector) against dense decode over the same
+    caches, both with this library's dense kernel and with torch SDPA (the reference's A path, sdpa_fold).
+
+    c2: Qwen3-0.6B, B = 1, an 8192-token prompt of uniform ids prefilled in 2048-token chunks (this builds the index
+        table), then 256 greedy steps (legal lengths 8193 .. 8448, k0 = 256).
+    c3: Qwen3-8B shape, 32K context per request, as many requests as the GPU holds next to the weights (at most 32).
+        The caches are filled with synthetic N(0,1) K/V and N(0, 0.23^2) index keys (a 32 x 32K-token prefill through
+        an 8B model is not part of the decode measurement), then greedy steps at legal lengths up to 32768.
+    Timing: CUDA events around the decode loop (device time; every step is a full model forward from token ids to
+    next-token logits and the greedy argmax, with the runner's host work in the loop); tokens/s = B x steps / time."""
+    import torch
+    from attention_lab_b200 import runner as rn
+    from attention_lab_b200.selection import fixed_budget
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    big = args.model == "c3"
+    cfg = rn.qwen3_config("8b" if big else "0.6b")
+    model = rn.random_qwen3(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    idt = torch.bfloat16 if args.index_dtype == "bf16" else torch.float32
+    n_params = sum(p.numel() for p in model.parameters())
+    holder = rn.wrap_model(model)
+    G, d, layers, V = cfg.num_key_value_heads, cfg.head_dim, cfg.num_hidden_layers, cfg.vocab_size
+    if big:
+        ctx, steps = 32768, args.model_steps or 16
+        cap = ctx
+        per_req = layers * (2 * G * cap * d * 2 + G * 32 * cap * (2 if idt == torch.bfloat16 else 4))
+        free = torch.cuda.mem_get_info(dev)[0]
+        B = int(max(1, min(32, (free - (6 << 30)) // per_req)))
+    else:
+        ctx, steps, B = 8192, args.model_steps or 256, 1
+        cap = ctx + steps
+    st = rn.make_state(model, cap, "sparse", batch=B, index_dtype=idt)
+    cache = st.cache
+    gen = torch.Generator(device=dev).manual_seed(5)
+    with torch.inference_mode():
+        if big:
+            start = ctx - steps
+            for l in range(layers):
+                cache.k[l].normal_(0.0, 1.0, generator=gen)
+                cache.v[l].normal_(0.0, 1.0, generator=gen)
+                cache.z[l].normal_(0.0, 0.23, generator=gen)
+            cache.valid_length = start
+        else:
+            prompt = torch.randint(0, 151643, (B, ctx), generator=gen, device=dev)
+            rn.LabRunner(model, holder, st).prefill(prompt, 2048)
+            start = ctx
+    dense = rn.LabCache.__new__(rn.LabCache)             # the same K/V buffers, without the index table
+    dense.__dict__.update(cache.__dict__)
+    dense.z, dense.index_dim = None, None
+    dense.writes, dense.last_write = list(cache.writes), list(cache.last_write)
+    first = torch.randint(0, 151643, (B, 1), generator=gen, device=dev)
+
+    def decode(state, n):
+        run = rn.LabRunner(model, holder, state)
+        state.cache.rollback(start)
+        if state.mode == "sparse":
+            state.begin_request(1 / 32)
+        tok = first
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        e0.record()
+        for _ in range(n):
+            tok = run.step(tok).argmax(dim=-1)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n, (time.perf_counter() - t0) * 1e3 / n
+
+    def graphed(state, n):
+        """One decode step at legal length start + 1 (model forward, the read, greedy argmax written back into the
+        step's input) captured as a CUDA graph, replayed n times: every replay is a whole decode step at that
+        context (slot `start` is rewritten each time), with no host work between steps."""
+        run = rn.LabRunner(model, holder, state)
+        tok = first.clone()
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                state.cache.rollback(start)
+                if state.mode == "sparse":
+                    state.begin_request(1 / 32)
+                tok.copy_(run.step(tok).argmax(dim=-1))
+        torch.cuda.current_stream(dev).wait_stream(side)
+        state.cache.rollback(start)
+        if state.mode == "sparse":
+            state.begin_request(1 / 32)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            tok.copy_(run.step(tok).argmax(dim=-1))
+        state.cache.rollback(start)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        del graph
+        return e0.elapsed_time(e1) / n
+
+    res = {}
+    with torch.inference_mode():
+        for name, state in (("sparse", st), ("dense_kernel", rn.LabState(dense, None, mode="full")),
+                            ("dense_sdpa", rn.LabState(dense, None, mode="full", decode_backend="sdpa_fold"))):
+            decode(state, min(3, steps))                  # warm-up
+            ms, wall = decode(state, steps)
+            res[name] = {"tokens_per_s": round(B / (ms / 1e3), 2), "ms_per_step": round(ms, 3),
+                         "wall_ms_per_step": round(wall, 3)}
+            if args.model_graph:
+                gms = graphed(state, max(steps, 10))
+                res[name]["graph_tokens_per_s"] = round(B / (gms / 1e3), 2)
+                res[name]["graph_ms_per_step"] = round(gms, 3)
+    k0 = fixed_budget(start + 1, 1 / 32)
+    line = {"metric": f"end-to-end decode tokens/s, random-init Qwen3-{'8B shape' if big else '0.6B'} ({args.model.upper()})",
+            "value": res["sparse"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": (f"{args.model.upper()}: {layers} layers, hidden {cfg.hidden_size}, "
+                                    f"{cfg.num_attention_heads}/{G} heads, d {d}, vocab {V}, B {B}, context up to "
+                                    f"{start + steps}, rho 1/32 (k0 {k0}), index {args.index_dtype}"),
+                       "batch": B, "parameters": n_params, "cache_capacity": cap,
+                       "caches": "synthetic fill" if big else "prefilled from an 8192-token prompt (chunks of 2048)",
+                       "cuda_graph": False},
+            "modes": res,
+            "speedup_vs_dense_sdpa": round(res["sparse"]["tokens_per_s"] / res["dense_sdpa"]["tokens_per_s"], 3),
+            "speedup_vs_dense_kernel": round(res["sparse"]["tokens_per_s"] / res["dense_kernel"]["tokens_per_s"], 3)}
+    if args.model_graph:
+        g = {k: v["graph_tokens_per_s"] for k, v in res.items()}
+        line["graph"] = {"what": f"one decode step at legal length {start + 1} captured as a CUDA graph and replayed "
+                                 "(no host work between steps)",
+                         "sparse_tokens_per_s": g["sparse"],
+                         "speedup_vs_dense_sdpa": round(g["sparse"] / g["dense_sdpa"], 3),
+                         "speedup_vs_dense_kernel": round(g["sparse"] / g["dense_kernel"], 3)}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def cpu_prefill_sample(H, T, k, budget_s):
     """The whole C5 chunk (H heads x T rows) through oracle.cpu_prefill_rows (float32 numpy), blocks of 256 rows in
     parallel over the host cores (one BLAS thread each); repeated until ~budget_s. Returns query rows/s."""
@@ -488,6 +633,8 @@ def main():
         return run_context_split(args)
     if args.prefill:
         return run_prefill(args)
+    if args.model:
+        return run_model(args)
     import torch
     import torch.distributed as dist
     import attention_lab_b200 as al
