@@ -203,10 +203,9 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 std::unordered_map<unsigned long long, CUtensorMap> g_zmaps;
 
-bool zt_tensor_map(const void* zT, int idx_dtype, long long rows, int C, CUtensorMap* out) {
+EncodeTiledFn tensor_map_encoder() {   // called with g_mu held
   static EncodeTiledFn enc = nullptr;
   static bool tried = false;
-  std::lock_guard<std::mutex> lk(g_mu);
   if (!tried) {
     tried = true;
     cudaDriverEntryPointQueryResult q;
@@ -215,6 +214,12 @@ bool zt_tensor_map(const void* zT, int idx_dtype, long long rows, int C, CUtenso
         q == cudaDriverEntryPointSuccess)
       enc = reinterpret_cast<EncodeTiledFn>(fn);
   }
+  return enc;
+}
+
+bool zt_tensor_map(const void* zT, int idx_dtype, long long rows, int C, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const EncodeTiledFn enc = tensor_map_encoder();
   if (!enc) return false;
   const unsigned long long key = reinterpret_cast<unsigned long long>(zT) ^ ((unsigned long long)C << 1) ^
                                  ((unsigned long long)rows << 29) ^ ((unsigned long long)idx_dtype << 62);
@@ -232,6 +237,34 @@ bool zt_tensor_map(const void* zT, int idx_dtype, long long rows, int C, CUtenso
   if (r != CUDA_SUCCESS) return false;
   if (g_zmaps.size() > 4096) g_zmaps.clear();
   g_zmaps[key] = m;
+  *out = m;
+  return true;
+}
+
+// Tensor map of the prefill scorer's zT [H, 32, C] (bf16, element strides z_sh, z_ld): boxes of 64 columns x 32 rows
+// x 1 head with the 128-byte swizzle, the N-major operand layout of the tensor-core MMA. Cached like zt_tensor_map.
+std::unordered_map<unsigned long long, CUtensorMap> g_pfmaps;
+
+bool pf_tensor_map(const void* zT, int H, int C, long long z_sh, long long z_ld, CUtensorMap* out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  const EncodeTiledFn enc = tensor_map_encoder();
+  if (!enc) return false;
+  const unsigned long long key = reinterpret_cast<unsigned long long>(zT) ^ ((unsigned long long)C << 1) ^
+                                 ((unsigned long long)H << 20) ^ ((unsigned long long)z_sh << 30) ^
+                                 ((unsigned long long)z_ld << 47);
+  auto it = g_pfmaps.find(key);
+  if (it != g_pfmaps.end()) { *out = it->second; return true; }
+  cuuint64_t dims[3] = {(cuuint64_t)C, 32u, (cuuint64_t)H};
+  cuuint64_t strides[2] = {(cuuint64_t)z_ld * 2u, (cuuint64_t)z_sh * 2u};
+  cuuint32_t box[3] = {64u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUtensorMap m;
+  const CUresult r = enc(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(zT), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (g_pfmaps.size() > 4096) g_pfmaps.clear();
+  g_pfmaps[key] = m;
   *out = m;
   return true;
 }
@@ -698,7 +731,7 @@ int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const v
   if (!u || !zT || !idx_out) return fail(AL_EINVAL, "null pointer argument");
   if (r != kPfR) return fail(AL_EUNSUPPORTED, "index dimension r must be %d, got %d", kPfR, r);
   if (H <= 0 || T <= 0 || C <= 0) return fail(AL_EINVAL, "H, T and C must be positive");
-  if (H > 65535) return fail(AL_EUNSUPPORTED, "at most 65535 heads");
+  if (H > 65535 || (T + kPfRows - 1) / kPfRows > 65535) return fail(AL_EUNSUPPORTED, "at most 65535 heads and 65535 row tiles");
   if (q_pos0 < 0) return fail(AL_EINVAL, "negative first query position");
   if ((long long)q_pos0 + T > C) return fail(AL_EINVAL, "query positions [%d, %lld) exceed the table's %d columns", q_pos0,
                                              (long long)q_pos0 + T, C);
@@ -710,14 +743,20 @@ int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const v
     return fail(AL_EUNSUPPORTED, "zT needs 16-byte aligned rows (C, row and head strides multiples of 8)");
   if (z_ld < C || u_st < kPfR) return fail(AL_EINVAL, "strides smaller than the rows they step over");
   if (u_st % 2 || u_sh % 2 || (reinterpret_cast<uintptr_t>(u) & 3)) return fail(AL_EUNSUPPORTED, "u needs 4-byte aligned rows");
-  int rc = prepare_kernel(prefill_topk_kernel, kPfSmem, 1);
+  if (reinterpret_cast<uintptr_t>(scores_out) & 15) return fail(AL_EUNSUPPORTED, "scores_out must start on a 16-byte boundary");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  CUtensorMap zmap;
+  if (!pf_tensor_map(zT, H, C, z_sh, z_ld, &zmap)) return fail(AL_ECUDA, "cuTensorMapEncodeTiled refused the zT layout");
+  rc = prepare_kernel(prefill_topk_kernel, kPfSmem, 1);
   if (rc) return rc;
   PrefillParams p{};
   p.u = static_cast<const __nv_bfloat16*>(u); p.u_sh = u_sh; p.u_st = u_st;
-  p.zT = static_cast<const __nv_bfloat16*>(zT); p.z_sh = z_sh; p.z_ld = z_ld;
   p.T = T; p.C = C; p.q_pos0 = q_pos0; p.k = k; p.kcap = kcap; p.idx = idx_out; p.scores = scores_out;
-  const dim3 grid((unsigned)((T + kPfRows - 1) / kPfRows), (unsigned)H);
-  prefill_topk_kernel<<<grid, kThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(p);
+  p.err = di->err;
+  const dim3 grid((unsigned)H, (unsigned)((T + kPfRows - 1) / kPfRows));
+  prefill_topk_kernel<<<grid, kPfThreads, kPfSmem, static_cast<cudaStream_t>(stream)>>>(p, zmap);
   return plain_launch_check("prefill_topk_kernel");
 }
 

@@ -4,311 +4,586 @@
 // decode.py:86-93 applied to every query row of the chunk at once. The reference selects nothing in prefill
 // (qwen_wrap.py:287-289); this is the batched form of its decode-time selection.
 //
-// One CTA serves 16 query rows of one head (one m16 tile) and sweeps the columns its rows can see in tiles of
-// 128: the zT tile is staged in shared memory by cp.async, each warp computes 16 rows x 16 columns of fp32 scores
-// with bf16 mma.sync (K = 32: two k-steps), and turns them into order-preserving uint32 keys. Keys are never
-// stored; each sweep recomputes them (the MMA is deterministic, so every sweep sees the same keys):
-//   sweep 0: per-row histogram of the top 11 key bits        -> pivot bin, how many above it
-//   sweep 1: histogram of bits 20..10 of keys in that bin     -> skipped for rows already resolved
-//   sweep 2: histogram of bits 9..0                           -> skipped for rows already resolved
-//   sweep 3: emission: keys above the pivot prefix, plus the first `need` keys equal to it in position order,
-//            written in ascending position order.
-// A row is resolved once its pivot bin holds exactly the keys it still needs (usual after sweep 1 for continuous
-// scores); rows with M(p) <= k take every candidate and skip the histogram sweeps.
+// One CTA serves 128 query rows of one head: the tensor cores compute a 128 x 128 tile of scores per step
+// (tcgen05.mma, kind::f16, bf16 operands from shared memory, fp32 accumulators in tensor memory), zT tiles arrive by
+// TMA (128-byte swizzle, the layout the MMA reads as an N-major operand) in a 4-stage ring, and the accumulators sit in
+// two 128-column TMEM buffers so the next tile is multiplied while the current one is read. Four warps read TMEM with
+// one thread per query row (TMEM lane = row), so every row's keys pass through one thread in position order; a fifth
+// warp issues the copies and the MMAs. Scores are never stored: each sweep over the columns recomputes them (the MMA
+// is deterministic, so every sweep sees the same values).
+//
+// Selection per row, on order-preserving integer keys of the scores:
+//   histogram sweep: 128 bins of 2^19 key units (1/16 of an octave) below an anchor taken from the row's first 32
+//                    candidates (twice their maximum), keys above it in bin 0, below the window in bin 127. The bin
+//                    holding the k-th largest key becomes the row's window.
+//   gather sweep:    the window's keys (at most 128) are copied to shared memory; one warp finds the exact k-th
+//                    largest among them (a bitwise select), and how many keys equal to it are still to be taken.
+//   emit sweep:      keys above the threshold, plus the first `need` keys equal to it, in position order.
+// A window holding more than 128 keys is split again by a finer histogram sweep (bins of 2^12, 2^5, 1 units). While
+// the row's scores are finite and the window lies above zero, the key of a score is its raw float bit pattern (an
+// order-preserving integer for positive floats); rows with a NaN or infinity, a non-positive anchor, or a window that
+// reaches zero switch to the canonical key (NaN above +inf, -0 = +0, negative scores ordered) and start over. Rows
+// with M(p) <= k take every candidate and skip to the emit sweep.
 #pragma once
+#include <climits>
+#include <cuda.h>
 #include "al_common.cuh"
 
 namespace al {
 
-constexpr int kPfRows = 16;          // query rows per CTA
-constexpr int kPfCols = 128;         // columns per tile
-constexpr int kPfR = 32;             // index dimension r
-constexpr int kPfRowPad = kPfCols + 8;   // padded tile row (bf16): ldmatrix rows land in distinct banks
-constexpr int kPfBins = 2048;        // 11-bit digits; packed two 16-bit counters per word
-constexpr int kPfHistWords = kPfRows * kPfBins / 2;
-constexpr int kPfStages = 4;         // zT tiles in flight: three ahead of the one being scored
-constexpr size_t kPfTileBytes = (size_t)kPfR * kPfRowPad * 2;
-constexpr size_t kPfSmem = (size_t)kPfHistWords * 4 + kPfStages * kPfTileBytes + 2 * kPfRows * 4 * 4;
+constexpr int kPfRows = 128;               // query rows per CTA: the MMA's M, one TMEM lane each
+constexpr int kPfTile = 128;               // columns per tile: the MMA's N
+constexpr int kPfR = 32;                   // index dimension r: the MMA's K (two kind::f16 steps of 16)
+constexpr int kPfStages = 4;               // zT tiles in flight (even: stage reuse tracks the TMEM buffer's barrier)
+constexpr int kPfRowWarps = 4;             // warps reading TMEM, one thread per query row
+constexpr int kPfThreads = 32 * (kPfRowWarps + 1);
+constexpr int kPfBins = 128;
+constexpr int kPfFirstShift = 19;          // first histogram: bins of 2^19 key units
+constexpr int kPfGather = 128;             // keys gathered per row
+constexpr int kPfStaged = 256;             // staged output positions per row (k <= 256)
+constexpr int kPfTmemCols = 2 * kPfTile;
+constexpr uint32_t kPfStageBytes = kPfR * kPfTile * 2;               // 8 KB: two 64-column boxes of 32 rows
+constexpr uint32_t kPfABytes = kPfRows * kPfR * 2;                   // 8 KB of u rows
+constexpr uint32_t kPfWorkBytes = kPfRows * kPfBins * 4;             // 64 KB: histogram / gather / staging
+constexpr size_t kPfSmem = 1024 + kPfStages * kPfStageBytes + kPfABytes + kPfWorkBytes;
+
+static_assert(kPfStages % 2 == 0, "stage s is reused by the tile that reuses its TMEM buffer");
+static_assert(kPfGather * kPfRows * 4 == kPfWorkBytes && kPfStaged * kPfRows * 2 == kPfWorkBytes, "work area");
+
+// Row states (one thread per row).
+constexpr int kPfNone = 0, kPfHist = 1, kPfGatherSt = 2, kPfEmit = 3, kPfDone = 4;
 
 struct PrefillParams {
   const __nv_bfloat16* u;      // [H, T, 32]
   long long u_sh, u_st;        // element strides of head and row
-  const __nv_bfloat16* zT;     // [H, 32, C]
-  long long z_sh, z_ld;        // element strides of head and index row
   int T, C, q_pos0, k, kcap;
   int* idx;                    // [H, T, kcap] positions, ascending, -1 past the row's count
   float* scores;               // optional [H, T, C] fp32 (candidate columns only)
+  unsigned* err;
 };
 
-__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(smem)), "l"(gmem),
-               "r"(valid ? 16 : 0) : "memory");
+// ------------------------------------------------------------------------------------------------ tcgen05 helpers
+// Shared-memory matrix descriptor (sm_100): start address, leading and stride byte offsets (all >> 4), version 1,
+// layout type in bits 61..63 (0 = no swizzle, 2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t pf_sdesc(uint32_t saddr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
 }
 
-__device__ __forceinline__ uint32_t pf_count(const uint32_t* h, int bin) {
-  return (h[bin >> 1] >> ((bin & 1) << 4)) & 0xffffu;
-}
+// Instruction descriptor of kind::f16: fp32 accumulator, bf16 A and B, A K-major, B N-major, M = 128, N = 128.
+constexpr uint32_t kPfIdesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kPfTile >> 3) << 17) |
+                              ((uint32_t)(kPfRows >> 4) << 24);
 
-// Pivot of one row's histogram (one warp): the bin b with (count above b) < need <= (count at or above b).
-__device__ __forceinline__ void pf_pivot(const uint32_t* h, int nbins, uint32_t need, int lane, uint32_t& bin,
-                                         uint32_t& above, uint32_t& in_bin) {
-  const int per = nbins / 32;
-  const int top = nbins - per * lane;            // lane 0 covers the highest bins
-  uint32_t sum = 0;
-  for (int i = top - per; i < top; i += 2) {
-    const uint32_t w = h[i >> 1];
-    sum += (w & 0xffffu) + (w >> 16);
-  }
-  uint32_t incl = sum;
+__device__ __forceinline__ void pf_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+               " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+               ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kPfIdesc), "r"(accumulate) : "memory");
+}
+// Arrive once on `bar` when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void pf_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n"
+               ::"r"((uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+__device__ __forceinline__ void pf_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"((uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+// 3-D tiled bulk copy (x = column, y = index row, z = head) completing on `bar`; x * 2 bytes is a multiple of 128.
+__device__ __forceinline__ void pf_tma3(uint32_t dst, const void* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
+               ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z),
+               "r"((uint32_t)__cvta_generic_to_shared(bar)) : "memory");
+}
+// 32 consecutive TMEM columns of the thread's lane; the values are defined after pf_tmem_wait.
+__device__ __forceinline__ void pf_tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                 "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+                 "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+                 "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+               : "r"(taddr) : "memory");
+}
+// Wait for this thread's TMEM loads; the empty statements tie every loaded register to the wait so no use of them
+// is scheduled before it.
+__device__ __forceinline__ void pf_tmem_wait(uint32_t (&v)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  const uint32_t excl = incl - sum;
-  const unsigned hit = __ballot_sync(0xffffffffu, excl < need && incl >= need);
-  const int src = hit ? __ffs(hit) - 1 : 0;
-  uint32_t b = 0, a = 0, c = 0;
-  if (lane == src) {
-    uint32_t acc = excl;
-    for (int i = top - 1; i >= top - per; --i) {
-      const uint32_t n = pf_count(h, i);
-      if (acc + n >= need) { b = (uint32_t)i; a = acc; c = n; break; }
-      acc += n;
+  for (int j = 0; j < 32; ++j) asm volatile("" : "+r"(v[j]));
+}
+
+// ------------------------------------------------------------------------------------------------ keys
+// Canonical key (signed order): NaN above +inf, -0 = +0, negative scores below every non-negative one. On positive
+// finite scores it equals the raw bit pattern, which is what rows in the fast mode use.
+__device__ __forceinline__ int pf_canon(uint32_t v) {
+  const float s = __uint_as_float(v);
+  if (s != s) return INT_MAX;
+  if (s == 0.0f) return 0;
+  return (v & 0x80000000u) ? (int)(v ^ 0x7fffffffu) : (int)v;
+}
+
+struct PfRow {
+  int lo, hi;            // candidate columns [lo, hi)
+  int kk;                // keys to choose: min(k, hi - lo)
+  int state;
+  bool gen;              // canonical keys
+  int need;              // keys still to choose inside the window
+  int top, sh;           // histogram: bin (top - min(key, top)) >> sh, capped at 127
+  int wlo, whi;          // window of keys (inclusive) that still holds the threshold
+  int thr, eqleft;       // emission: keys above thr, then the first eqleft keys equal to it
+  bool tie;              // eqleft is below the number of keys equal to thr
+  int cnt;               // gathered keys, then emitted positions
+  float sum;             // first histogram sweep, fast mode: non-finite sum = a NaN or infinity in the row
+};
+
+// Restart a row's selection in the canonical-key mode over the whole key range.
+__device__ __forceinline__ void pf_restart_canonical(PfRow& r) {
+  r.gen = true;
+  r.state = kPfHist;
+  r.need = r.kk;
+  r.top = INT_MAX; r.sh = 25;          // (INT_MAX - key) >> 25 covers all 2^32 keys in 128 bins
+  r.wlo = INT_MIN; r.whi = INT_MAX;
+}
+
+__device__ __forceinline__ void pf_red_add(uint32_t saddr) {
+  asm volatile("red.shared.add.u32 [%0], 1;\n" ::"r"(saddr) : "memory");
+}
+__device__ __forceinline__ void pf_st32(uint32_t saddr, int v) {
+  asm volatile("st.shared.b32 [%0], %1;\n" ::"r"(saddr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void pf_st16(uint32_t saddr, int v) {
+  asm volatile("st.shared.u16 [%0], %1;\n" ::"r"(saddr), "h"((unsigned short)v) : "memory");
+}
+__device__ __forceinline__ uint32_t pf_ld32(uint32_t saddr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];\n" : "=r"(v) : "r"(saddr) : "memory");
+  return v;
+}
+__device__ __forceinline__ int pf_ld16(uint32_t saddr) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(v) : "r"(saddr) : "memory");
+  return (int)v;
+}
+
+
+// One 32-column chunk of a row's scores v (columns c0 .. c0 + 31), of which [jlo, jhi) are candidates unless FULL.
+//   KIND kPfHist:     count each key of the window in the row's histogram (hist: this row's bin-0 word; bins are
+//                     512 bytes apart). FIRST: the row's first sweep (whole key range; fast mode adds up the scores).
+//   KIND kPfGatherSt: append the window's keys to the row's list (work: the row's 512-byte slot).
+//   KIND kPfEmit:     append the chosen positions (TIE: only the first eqleft keys equal to thr are taken) to the
+//                     row's staged list (16-bit, in work) or straight to its output row.
+// Key differences are taken in unsigned arithmetic (windows may span the whole signed range).
+template <int KIND, bool GEN, bool FULL, bool FIRST, bool TIE>
+__device__ __forceinline__ void pf_chunk(const uint32_t (&v)[32], int c0, int jlo, int jhi, PfRow& r, uint32_t hist,
+                                         uint32_t work, int* out, bool staged) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (!FULL && (j < jlo || j >= jhi)) continue;
+    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
+    if (KIND == kPfHist) {
+      if (FIRST && !GEN) r.sum += __uint_as_float(v[j]);
+      if (!FIRST && (unsigned)key - (unsigned)r.wlo > (unsigned)r.whi - (unsigned)r.wlo) continue;
+      const unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> r.sh, (unsigned)(kPfBins - 1));
+      pf_red_add(hist + (d << 9));
+    } else if (KIND == kPfGatherSt) {
+      if ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) {
+        if (r.cnt < kPfGather) pf_st32(work + ((uint32_t)r.cnt << 2), key);
+        ++r.cnt;
+      }
+    } else {
+      bool take;
+      if (TIE) {
+        const bool eq = key == r.thr;
+        take = key > r.thr || (eq && r.eqleft > 0);
+        if (eq && take) --r.eqleft;
+      } else {
+        take = key >= r.thr;
+      }
+      if (take) {
+        if (r.cnt < r.kk) {                     // always, unless the launch was flagged invalid
+          if (staged) pf_st16(work + ((uint32_t)r.cnt << 1), c0 + j);
+          else out[r.cnt] = c0 + j;
+        }
+        ++r.cnt;
+      }
     }
   }
-  bin = __shfl_sync(0xffffffffu, b, src);
-  above = __shfl_sync(0xffffffffu, a, src);
-  in_bin = __shfl_sync(0xffffffffu, c, src);
 }
 
-__global__ void __launch_bounds__(kThreads, 2) prefill_topk_kernel(PrefillParams p) {
-  extern __shared__ __align__(128) unsigned char pf_smem[];
-  uint32_t* hist = reinterpret_cast<uint32_t*>(pf_smem);
-  __nv_bfloat16* tiles = reinterpret_cast<__nv_bfloat16*>(pf_smem + (size_t)kPfHistWords * 4);
-  uint32_t* m_gt = reinterpret_cast<uint32_t*>(pf_smem + (size_t)kPfHistWords * 4 + kPfStages * kPfTileBytes);
-  uint32_t* m_eq = m_gt + kPfRows * 4;
-  __shared__ int s_lo[kPfRows], s_hi[kPfRows], s_shift[kPfRows], s_eqb[kPfRows], s_outb[kPfRows];
-  __shared__ uint32_t s_pref[kPfRows], s_need[kPfRows];
-  __shared__ int s_state[kPfRows];   // 0 no candidates or taken whole; 1 refining; 2 resolved
-  __shared__ int s_any;
+// The row's anchor, from the candidates of its first chunk: twice their largest score. A row without a positive
+// finite maximum there uses canonical keys from the start.
+__device__ __forceinline__ void pf_anchor(const uint32_t (&v)[32], int jlo, int jhi, PfRow& r) {
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j >= jlo && j < jhi) m = fmaxf(m, __uint_as_float(v[j]));
+  if (m > 0.0f && m <= 3.402823466e38f) {
+    r.gen = false;
+    r.top = __float_as_int(2.0f * m);
+    r.sh = kPfFirstShift;
+    r.wlo = INT_MIN; r.whi = INT_MAX;
+    r.need = r.kk;
+    r.sum = 0.0f;
+  } else {
+    pf_restart_canonical(r);
+  }
+}
 
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int head = blockIdx.y;
-  const int tile_row = (int)gridDim.x - 1 - (int)blockIdx.x;     // the longest rows start first
-  const int t0 = tile_row * kPfRows;
-  const __nv_bfloat16* zT = p.zT + (size_t)head * p.z_sh;
+// Bounded wait; after the first wait that gives up, the CTA stops waiting (its results are invalid and flagged).
+__device__ __forceinline__ void pf_wait(uint64_t* bar, unsigned parity, volatile int* abort_flag, unsigned* err) {
+  if (*abort_flag) return;
+  if (!mbar_wait(bar, parity)) {
+    *abort_flag = 1;
+    atomicOr(err, kErrWaitLimit);
+  }
+}
 
-  if (tid < kPfRows) {
-    const int t = t0 + tid;
-    int lo = 0, hi = 0, kk = 0;
+template <int KIND, bool GEN, bool FULL, bool FIRST>
+__device__ __forceinline__ void pf_chunk_tie(const uint32_t (&v)[32], int c0, int jlo, int jhi, PfRow& r, uint32_t hist,
+                                             uint32_t work, int* out, bool staged) {
+  if (KIND == kPfEmit && r.tie) pf_chunk<KIND, GEN, FULL, FIRST, true>(v, c0, jlo, jhi, r, hist, work, out, staged);
+  else pf_chunk<KIND, GEN, FULL, FIRST, false>(v, c0, jlo, jhi, r, hist, work, out, staged);
+}
+
+template <int KIND, bool FIRST>
+__device__ __forceinline__ void pf_dispatch(const uint32_t (&v)[32], int c0, int jlo, int jhi, bool full, PfRow& r,
+                                            uint32_t hist, uint32_t work, int* out, bool staged) {
+  if (r.gen) {
+    if (full) pf_chunk_tie<KIND, true, true, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
+    else pf_chunk_tie<KIND, true, false, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
+  } else {
+    if (full) pf_chunk_tie<KIND, false, true, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
+    else pf_chunk_tie<KIND, false, false, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
+  }
+}
+
+// One sweep of a row thread over nt tiles of TMEM scores (global tile counter g). Rows in state KIND do that sweep's
+// work; in the CTA's first sweep every row with candidates also writes its scores when asked to.
+template <int KIND>
+__device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, uint32_t tcol, uint64_t* tfull, uint64_t* tfree,
+                         uint32_t hist, uint32_t work, int* out, float* srow, bool staged, volatile int* abort_flag,
+                         unsigned* err) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int i = 0; i < nt; ++i, ++g) {
+    const int buf = g & 1;
+    pf_wait(&tfull[buf], (unsigned)(g >> 1) & 1u, abort_flag, err);
+    tmem_fence_after_sync();
+    const int c0 = i * kPfTile;
+    const bool act = r.state == KIND;
+    const bool wscore = first && srow != nullptr && r.hi > r.lo;
+#pragma unroll 1
+    for (int q = 0; q < kPfTile / 32; ++q) {
+      uint32_t v[32];
+      pf_tmem_ld32(tcol + (uint32_t)(buf * kPfTile + q * 32), v);
+      pf_tmem_wait(v);
+      if (q == kPfTile / 32 - 1) {             // the buffer is in registers: the MMA may overwrite it
+        tmem_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) pf_arrive(&tfree[buf]);
+      }
+      const int cq = c0 + 32 * q;
+      const int jlo = r.lo - cq, jhi = r.hi - cq;       // candidates of this chunk: [jlo, jhi) clipped to [0, 32)
+      if (jhi <= 0 || jlo >= 32) continue;
+      const bool full = jlo <= 0 && jhi >= 32;
+      if (wscore) {
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(srow + cq + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                    __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (j >= jlo && j < jhi) srow[cq + j] = __uint_as_float(v[j]);
+        }
+      }
+      if (KIND == kPfNone || !act) continue;
+      if (KIND == kPfHist && first) {
+        if (i == 0 && q == 0) pf_anchor(v, jlo, jhi, r);
+        pf_dispatch<KIND, true>(v, cq, jlo, jhi, full, r, hist, work, out, staged);
+      } else {
+        pf_dispatch<KIND, false>(v, cq, jlo, jhi, full, r, hist, work, out, staged);
+      }
+    }
+  }
+}
+
+// After a histogram sweep: the bin holding the row's need-th largest key (counting from the top) becomes the window;
+// the row's 128 bins are cleared on the way. `first`: the row's first sweep, after which a fast-mode row whose scores
+// did not sum to a finite value (a NaN or an infinity among them) starts over with canonical keys.
+__device__ __forceinline__ void pf_after_hist(PfRow& r, uint32_t hist, bool first) {
+  unsigned cum = 0, before = 0, inb = 0;
+  int piv = -1;
+#pragma unroll 8
+  for (int d = 0; d < kPfBins; ++d) {
+    const unsigned c = pf_ld32(hist + ((uint32_t)d << 9));
+    pf_st32(hist + ((uint32_t)d << 9), 0);
+    if (piv < 0 && cum + c >= (unsigned)r.need) { piv = d; before = cum; inb = c; }
+    cum += c;
+  }
+  if (first && !r.gen && !isfinite(r.sum)) { pf_restart_canonical(r); return; }
+  if (piv < 0) { piv = kPfBins - 1; before = cum; inb = 0; }   // unreachable: the window holds the need-th key
+  const long long top = r.top;
+  long long hk = piv == 0 ? (long long)r.whi : top - ((long long)piv << r.sh);
+  long long lk = piv == kPfBins - 1 ? (long long)r.wlo : top - ((long long)(piv + 1) << r.sh) + 1;
+  hk = hk < r.whi ? hk : (long long)r.whi;
+  lk = lk > r.wlo ? lk : (long long)r.wlo;
+  r.need -= (int)before;
+  if (!r.gen && lk <= 0) { pf_restart_canonical(r); return; }
+  if (hk == lk) {                                   // a single key value: it is the threshold
+    r.state = kPfEmit; r.thr = (int)hk; r.eqleft = r.need; r.tie = r.need < (int)inb; r.cnt = 0;
+  } else if (inb <= (unsigned)kPfGather) {
+    r.state = kPfGatherSt; r.wlo = (int)lk; r.whi = (int)hk; r.cnt = 0;
+  } else {                                          // too many keys to gather: a finer histogram of the window
+    const unsigned long long span = (unsigned long long)(hk - lk);
+    const int bits = 64 - __clzll((long long)span);
+    r.wlo = (int)lk; r.whi = (int)hk; r.top = (int)hk; r.sh = bits > 7 ? bits - 7 : 0;
+  }
+}
+
+// After a gather sweep, one warp per row of its 32: the exact need-th largest of the gathered keys (an MSB-first
+// bitwise select on the offsets whi - key), the threshold and how many keys equal to it the row still takes.
+__device__ __forceinline__ void pf_after_gather(PfRow& r, uint32_t work_warp) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int rr = 0; rr < 32; ++rr) {
+    if (__shfl_sync(0xffffffffu, r.state, rr) != kPfGatherSt) continue;
+    const int n = __shfl_sync(0xffffffffu, r.cnt, rr);
+    const int need = __shfl_sync(0xffffffffu, r.need, rr);
+    const int whi = __shfl_sync(0xffffffffu, r.whi, rr);
+    const int wlo = __shfl_sync(0xffffffffu, r.wlo, rr);
+    const uint32_t row = work_warp + (uint32_t)rr * (kPfGather * 4);
+    unsigned o[kPfGather / 32];
+    bool ok[kPfGather / 32];
+#pragma unroll
+    for (int q = 0; q < kPfGather / 32; ++q) {
+      const int i = lane + 32 * q;
+      ok[q] = i < n;
+      o[q] = ok[q] ? (unsigned)whi - pf_ld32(row + (uint32_t)i * 4) : 0u;
+    }
+    const unsigned span = (unsigned)whi - (unsigned)wlo;
+    unsigned pref = 0;
+    int rem = need;
+#pragma unroll 1
+    for (int bit = 31 - __clz((int)(span | 1u)); bit >= 0; --bit) {
+      int c = 0;
+#pragma unroll
+      for (int q = 0; q < kPfGather / 32; ++q) c += (ok[q] && ((o[q] ^ pref) >> bit) == 0u) ? 1 : 0;
+      c = (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
+      if (c < rem) { rem -= c; pref |= 1u << bit; }
+    }
+    int gt = 0, eq = 0;
+#pragma unroll
+    for (int q = 0; q < kPfGather / 32; ++q) {
+      gt += (ok[q] && o[q] < pref) ? 1 : 0;
+      eq += (ok[q] && o[q] == pref) ? 1 : 0;
+    }
+    gt = (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);
+    eq = (int)__reduce_add_sync(0xffffffffu, (unsigned)eq);
+    if (lane == rr) {
+      r.state = kPfEmit;
+      r.thr = (int)((unsigned)whi - pref);
+      r.eqleft = need - gt;
+      r.tie = r.eqleft < eq;
+      r.cnt = 0;
+    }
+  }
+}
+
+
+// Grid (H, ceil(T / 128)), 160 threads: warps 0-3 hold one query row per thread, warp 4 issues TMA copies and MMAs.
+__global__ void __launch_bounds__(kPfThreads, 2)
+    prefill_topk_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap zmap) {
+  extern __shared__ __align__(1024) unsigned char pf_raw[];
+  __shared__ uint64_t s_full[kPfStages], s_tfull[2], s_tfree[2];
+  __shared__ uint32_t s_taddr;
+  __shared__ int s_nt, s_kind, s_flags, s_maxhi[4];
+  __shared__ volatile int s_abort;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int head = blockIdx.x;
+  const int t0 = ((int)gridDim.y - 1 - (int)blockIdx.y) * kPfRows;      // the longest rows of every head start first
+  const uint32_t raw = smem_addr(pf_raw);
+  const uint32_t sb = (raw + 1023u) & ~1023u;                             // 128-byte swizzle atoms: 1 KB aligned
+  const uint32_t s_stage = sb;
+  const uint32_t s_a = sb + kPfStages * kPfStageBytes;
+  const uint32_t s_work = s_a + kPfABytes;
+
+  if (tid == 0) {
+    for (int s = 0; s < kPfStages; ++s) mbar_init(&s_full[s], 1);
+    for (int b = 0; b < 2; ++b) { mbar_init(&s_tfull[b], 1); mbar_init(&s_tfree[b], kPfRowWarps); }
+    mbar_init_fence();
+    s_abort = 0; s_flags = 0;
+    for (int i = 0; i < 4; ++i) s_maxhi[i] = 0;
+  }
+  if (warp == 0) { tmem_alloc(&s_taddr, kPfTmemCols); tmem_relinquish(); }
+
+  PfRow r;
+  r.lo = 0; r.hi = 0; r.kk = 0; r.state = kPfNone; r.gen = false; r.need = 0; r.top = INT_MAX; r.sh = 25;
+  r.wlo = INT_MIN; r.whi = INT_MAX; r.thr = INT_MIN; r.eqleft = 0; r.tie = false; r.cnt = 0; r.sum = 0.0f;
+  const int t = t0 + tid;
+  const bool row_thread = warp < kPfRowWarps;
+  if (row_thread) {
+    // u row -> the MMA's A operand: K-major, no swizzle: 8 x (8 bf16) core matrices, K chunks 128 B apart, 8-row
+    // groups 512 B apart. Rows past the chunk are zero.
+#pragma unroll
+    for (int kc = 0; kc < kPfR / 8; ++kc) {
+      uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+      if (t < p.T) {
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.u + (size_t)head * p.u_sh + (size_t)t * p.u_st + kc * 8);
+        w0 = src[0]; w1 = src[1]; w2 = src[2]; w3 = src[3];
+      }
+      const uint32_t dst = s_a + (uint32_t)(tid >> 3) * 512u + (uint32_t)kc * 128u + (uint32_t)(tid & 7) * 16u;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
+    }
+    for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += kPfRows * 16u)
+      asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};\n" ::"r"(s_work + o), "r"(0) : "memory");
     if (t < p.T) {
       const int L = p.q_pos0 + t + 1;
-      lo = min(4, L);
-      hi = max(lo, L - 64);
-      kk = min(p.k, hi - lo);
-    }
-    s_lo[tid] = lo; s_hi[tid] = hi;
-    s_eqb[tid] = 0; s_outb[tid] = 0;
-    const bool whole = kk == hi - lo;          // every candidate is taken (or there are none)
-    s_state[tid] = (whole || kk == 0) ? 0 : 1;
-    // whole rows: every key is above prefix 0; k = 0 rows: no key is above 0xffffffff
-    s_pref[tid] = (kk == 0 && !whole) ? 0xffffffffu : 0u;
-    s_need[tid] = (whole || kk == 0) ? 0u : (uint32_t)kk;
-    s_shift[tid] = 0;
-  }
-  for (int i = tid; i < kPfHistWords; i += kThreads) hist[i] = 0;
-  for (int i = tid; i < 2 * kPfRows * 4; i += kThreads) m_gt[i] = 0;
-  // -1 past each row's count
-  for (int i = tid; i < kPfRows * p.kcap; i += kThreads) {
-    const int r = i / p.kcap, j = i - r * p.kcap, t = t0 + r;
-    if (t < p.T) {
-      const int L = p.q_pos0 + t + 1, lo = min(4, L), hi = max(lo, L - 64);
-      if (j >= min(p.k, hi - lo)) p.idx[((size_t)head * p.T + t) * p.kcap + j] = -1;
+      r.lo = min(4, L);
+      r.hi = max(r.lo, L - 64);
+      r.kk = min(p.k, r.hi - r.lo);
+      if (r.kk == 0) r.state = kPfNone;
+      else if (r.kk == r.hi - r.lo) r.state = kPfEmit;        // every candidate: thr = INT_MIN takes them all
+      else r.state = kPfHist;                                  // the anchor of the first sweep sets the window
     }
   }
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");   // u rows visible to the tensor cores
+  tmem_fence_before_sync();
   __syncthreads();
+  tmem_fence_after_sync();
+  const uint32_t tbase = s_taddr;
 
-  int col_end = 0;
+  const bool staged = p.k <= kPfStaged;
+  const uint32_t hist = s_work + (uint32_t)tid * 4u;                         // bin d of this row: + d * 512
+  const uint32_t work = s_work + (uint32_t)tid * (kPfGather * 4);            // this row's gather / staging slot
+  int* out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
+  float* srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
+  const uint32_t tcol = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+  const uint64_t adesc0 = pf_sdesc(s_a, 128, 512, 0);
+
+  int g = 0;
+  bool first = true;
 #pragma unroll 1
-  for (int r = 0; r < kPfRows; ++r) col_end = max(col_end, s_hi[r]);
-  const int ntiles = (col_end + kPfCols - 1) / kPfCols;
-
-  // A fragments of the 16 query rows (rows past T are zero)
-  const int g = lane >> 2, t4 = lane & 3;
-  uint32_t a[2][4];
-  {
-    const __nv_bfloat16* u = p.u + (size_t)head * p.u_sh;
-    const int r0 = t0 + g, r1 = t0 + g + 8;
-#pragma unroll
-    for (int ks = 0; ks < 2; ++ks) {
-      const int kc = ks * 16 + 2 * t4;
-      a[ks][0] = r0 < p.T ? *reinterpret_cast<const uint32_t*>(u + (size_t)r0 * p.u_st + kc) : 0u;
-      a[ks][1] = r1 < p.T ? *reinterpret_cast<const uint32_t*>(u + (size_t)r1 * p.u_st + kc) : 0u;
-      a[ks][2] = r0 < p.T ? *reinterpret_cast<const uint32_t*>(u + (size_t)r0 * p.u_st + kc + 8) : 0u;
-      a[ks][3] = r1 < p.T ? *reinterpret_cast<const uint32_t*>(u + (size_t)r1 * p.u_st + kc + 8) : 0u;
+  for (;;) {
+    if (row_thread) {
+      // the next sweep: histogram while any row needs one, then gather, then emit; its columns reach the largest
+      // candidate end among the rows taking part (every row with candidates in a first sweep writing scores)
+      const int want = r.state == kPfHist ? 1 : r.state == kPfGatherSt ? 2 : r.state == kPfEmit ? 4 : 0;
+      const unsigned wor = __reduce_or_sync(0xffffffffu, (unsigned)want);
+      const int mh1 = (int)__reduce_max_sync(0xffffffffu, (unsigned)(want == 1 ? r.hi : 0));
+      const int mh2 = (int)__reduce_max_sync(0xffffffffu, (unsigned)(want == 2 ? r.hi : 0));
+      const int mh4 = (int)__reduce_max_sync(0xffffffffu, (unsigned)(want == 4 ? r.hi : 0));
+      const int mha = (int)__reduce_max_sync(0xffffffffu, (unsigned)r.hi);
+      if (lane == 0) {
+        atomicOr(&s_flags, (int)wor);
+        atomicMax(&s_maxhi[0], mh1); atomicMax(&s_maxhi[1], mh2); atomicMax(&s_maxhi[2], mh4);
+        atomicMax(&s_maxhi[3], mha);
+      }
+      asm volatile("bar.sync 1, %0;\n" ::"n"(kPfRows) : "memory");
+      if (tid == 0) {
+        const int f = s_flags;
+        const int kind = (f & 1) ? kPfHist : (f & 2) ? kPfGatherSt : (f & 4) ? kPfEmit : kPfNone;
+        int mh = kind == kPfHist ? s_maxhi[0] : kind == kPfGatherSt ? s_maxhi[1] : kind == kPfEmit ? s_maxhi[2] : 0;
+        if (first && p.scores) mh = max(mh, s_maxhi[3]);
+        if (s_abort) mh = 0;
+        s_kind = kind;
+        s_nt = (mh + kPfTile - 1) / kPfTile;
+        s_flags = 0;
+        for (int i = 0; i < 4; ++i) s_maxhi[i] = 0;
+      }
     }
+    __syncthreads();
+    const int nt = s_nt, kind = s_kind;
+    if (nt == 0) break;
+    if (!row_thread) {
+      if (lane == 0) {
+        // producer: TMA of zT tile gg (columns x .. x + 127 of this head) into stage gg % kPfStages, once the MMA of
+        // the tile that used the stage before (gg - kPfStages, same TMEM buffer) is complete; in a new sweep those
+        // MMAs finished before the row threads closed the previous one
+        const int gs = g;
+        auto issue = [&](int gg) {
+          const int s = gg % kPfStages;
+          if (gg - kPfStages >= gs)
+            pf_wait(&s_tfull[(gg - kPfStages) & 1], (unsigned)((gg - kPfStages) >> 1) & 1u, &s_abort, p.err);
+          mbar_arrive_expect_tx(&s_full[s], kPfStageBytes);
+          const uint32_t dst = s_stage + (uint32_t)s * kPfStageBytes;
+          const int x = (gg - gs) * kPfTile;
+          pf_tma3(dst, &zmap, x, 0, head, &s_full[s]);
+          pf_tma3(dst + kPfStageBytes / 2, &zmap, x + 64, 0, head, &s_full[s]);
+        };
+        for (int i = 0; i < min(nt, kPfStages - 1); ++i) issue(gs + i);
+#pragma unroll 1
+        for (int i = 0; i < nt; ++i) {
+          const int gg = gs + i, s = gg % kPfStages, buf = gg & 1;
+          pf_wait(&s_full[s], (unsigned)(gg / kPfStages) & 1u, &s_abort, p.err);
+          if (gg >= 2) pf_wait(&s_tfree[buf], (unsigned)((gg >> 1) - 1) & 1u, &s_abort, p.err);
+          tmem_fence_after_sync();
+          const uint32_t bst = s_stage + (uint32_t)s * kPfStageBytes;
+          // B: N-major, 128-byte swizzle; 64-column groups 4 KB apart, 8-row groups 1 KB apart; a K step of 16 rows
+          // advances B by 2 KB and A by 256 B
+#pragma unroll
+          for (int ks = 0; ks < kPfR / 16; ++ks)
+            pf_mma(tbase + (uint32_t)(buf * kPfTile), adesc0 + (uint64_t)((ks * 256) >> 4),
+                   pf_sdesc(bst + (uint32_t)ks * 2048u, kPfStageBytes / 2, 1024, 2), ks > 0 ? 1u : 0u);
+          pf_commit(&s_tfull[buf]);
+          if (i + kPfStages - 1 < nt) issue(gg + kPfStages - 1);
+        }
+      }
+      __syncwarp();
+      g += nt;
+    } else {
+      switch (kind) {
+        case kPfHist:
+          pf_sweep<kPfHist>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
+          if (r.state == kPfHist) pf_after_hist(r, hist, first);
+          break;
+        case kPfGatherSt:
+          pf_sweep<kPfGatherSt>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
+          __syncwarp();
+          pf_after_gather(r, s_work + (uint32_t)(32 * warp) * (kPfGather * 4));
+          break;
+        case kPfEmit:
+          pf_sweep<kPfEmit>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
+          if (r.state == kPfEmit) r.state = kPfDone;
+          break;
+        default:
+          pf_sweep<kPfNone>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
+          break;
+      }
+    }
+    first = false;
   }
 
-  auto load_tile = [&](int ti, int buf) {
-    const int c0 = ti * kPfCols;
-    __nv_bfloat16* dst = tiles + (size_t)buf * kPfR * kPfRowPad;
-#pragma unroll
-    for (int j = tid; j < kPfR * (kPfCols / 8); j += kThreads) {
-      const int row = j >> 4, ch = j & 15, c = c0 + ch * 8;
-      const bool ok = c + 8 <= p.C;
-      cp_async16_zfill(dst + row * kPfRowPad + ch * 8, ok ? (const void*)(zT + (size_t)row * p.z_ld + c) : (const void*)zT,
-                       ok);
-    }
-    cp_async_commit();
-  };
-
-  // sweeps 0..2 build histograms; sweep 3 emits
+  // the producer's last copies and MMAs, whatever happened to the waits above (bounded; complete already unless a wait
+  // gave up): nothing may still write this CTA's shared memory or tensor memory when it exits
+  if (!row_thread && lane == 0 && g > 0) {
+    for (int gg = max(0, g - kPfStages); gg < g; ++gg) mbar_wait(&s_full[gg % kPfStages], (unsigned)(gg / kPfStages) & 1u);
+    mbar_wait(&s_tfull[(g - 1) & 1], (unsigned)((g - 1) >> 1) & 1u);
+  }
+  // output rows: the staged positions (or the ones already written), then -1 up to kcap
+  if (row_thread) {
+    __syncwarp();
+    const int n_mine = (r.state == kPfDone) ? min(r.cnt, r.kk) : 0;
 #pragma unroll 1
-  for (int sweep = 0; sweep < 4; ++sweep) {
-    if (sweep < 3) {
-      if (tid == 0) {
-        int any = 0;
-        for (int r = 0; r < kPfRows; ++r) any |= s_state[r] == 1;
-        s_any = any;
+    for (int rr = 0; rr < 32; ++rr) {
+      const int tr = t0 + 32 * warp + rr;
+      const int n = __shfl_sync(0xffffffffu, n_mine, rr);
+      if (tr >= p.T) continue;
+      int* o = p.idx + ((size_t)head * p.T + tr) * p.kcap;
+      const uint32_t row = s_work + (uint32_t)(32 * warp + rr) * (kPfGather * 4);
+      if (staged) {
+        for (int j = lane; j < p.kcap; j += 32) o[j] = j < n ? pf_ld16(row + (uint32_t)j * 2) : -1;
+      } else {
+        for (int j = n + lane; j < p.kcap; j += 32) o[j] = -1;
       }
-      __syncthreads();
-      if (!s_any && !(sweep == 0 && p.scores)) continue;
     }
-    if (ntiles == 0) break;
-    // this thread's two rows (g and g + 8), read once per sweep; tiles wholly inside every row's candidate range
-    // skip the per-key range checks
-    int lo2[2], hi2[2], st2[2], sh2[2];
-    uint32_t pf2[2];
-    bool eq2[2];
-    int lo_max = 0, hi_min = 1 << 30;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int rr = g + 8 * h;
-      lo2[h] = s_lo[rr]; hi2[h] = s_hi[rr]; st2[h] = s_state[rr]; sh2[h] = s_shift[rr];
-      pf2[h] = s_pref[rr]; eq2[h] = s_need[rr] > 0;
-    }
-#pragma unroll 1
-    for (int r = 0; r < kPfRows; ++r) { lo_max = max(lo_max, s_lo[r]); hi_min = min(hi_min, s_hi[r]); }
-    const int sh_cmp = sweep == 1 ? 21 : 10;
-#pragma unroll
-    for (int st = 0; st < kPfStages - 1; ++st) {
-      if (st < ntiles) load_tile(st, st);
-      else cp_async_commit();
-    }
-#pragma unroll 1
-    for (int ti = 0; ti < ntiles; ++ti) {
-      // one group per tile, empty past the end: tile ti is complete once at most kPfStages - 1 groups are pending
-      if (ti + kPfStages - 1 < ntiles) load_tile(ti + kPfStages - 1, (ti + kPfStages - 1) % kPfStages);
-      else cp_async_commit();
-      cp_async_wait<kPfStages - 1>();
-      __syncthreads();
-      const __nv_bfloat16* buf = tiles + (size_t)(ti % kPfStages) * kPfR * kPfRowPad;
-      const int c0 = ti * kPfCols;
-      const bool interior = c0 >= lo_max && c0 + kPfCols <= hi_min;
-      float acc[2][4];
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-        const int n0 = warp * 16 + nb * 8;
-        uint32_t b0, b1, b2, b3;
-        ldmatrix_x4_trans(smem_addr(buf + (size_t)lane * kPfRowPad + n0), b0, b1, b2, b3);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nb][e] = 0.0f;
-        mma_bf16_16816(acc[nb], a[0][0], a[0][1], a[0][2], a[0][3], b0, b1);
-        mma_bf16_16816(acc[nb], a[1][0], a[1][1], a[1][2], a[1][3], b2, b3);
-      }
-#pragma unroll
-      for (int nb = 0; nb < 2; ++nb) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int h = e >> 1;
-          const int rr = g + 8 * h;
-          const int cl = warp * 16 + nb * 8 + 2 * t4 + (e & 1);
-          const int c = c0 + cl;
-          if (!interior && (c < lo2[h] || c >= hi2[h])) continue;
-          const uint32_t key = score_key(acc[nb][e]);
-          if (sweep == 0) {
-            if (p.scores) p.scores[((size_t)head * p.T + t0 + rr) * p.C + c] = acc[nb][e];
-            if (st2[h] == 1) {
-              const uint32_t d = key >> 21;
-              atomicAdd(&hist[rr * (kPfBins / 2) + (d >> 1)], 1u << ((d & 1) << 4));
-            }
-          } else if (sweep < 3) {
-            if (st2[h] == 1 && (key >> sh_cmp) == pf2[h]) {
-              const uint32_t d = sweep == 1 ? (key >> 10) & 2047u : key & 1023u;
-              atomicAdd(&hist[rr * (kPfBins / 2) + (d >> 1)], 1u << ((d & 1) << 4));
-            }
-          } else {
-            const uint32_t kp = key >> sh2[h];
-            if (kp > pf2[h]) atomicOr(&m_gt[rr * 4 + (cl >> 5)], 1u << (cl & 31));
-            else if (kp == pf2[h] && eq2[h]) atomicOr(&m_eq[rr * 4 + (cl >> 5)], 1u << (cl & 31));
-          }
-        }
-      }
-      if (sweep == 3) {
-        __syncthreads();
-        // row rr = tid / 16 emits its 8-column segment sg in position order
-        const int rr = tid >> 4, sg = tid & 15;
-        const int w = sg >> 2, sh = (sg & 3) * 8;
-        const uint32_t gt = (m_gt[rr * 4 + w] >> sh) & 0xffu, eq = (m_eq[rr * 4 + w] >> sh) & 0xffu;
-        const int neq = __popc(eq);
-        int eincl = neq;
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          const int t = __shfl_up_sync(0xffffffffu, eincl, o, 16);
-          if (sg >= o) eincl += t;
-        }
-        const int eq_before = s_eqb[rr] + eincl - neq;
-        const int room = max(0, (int)s_need[rr] - eq_before);
-        uint32_t take = eq;
-        for (int j = 0, seen = 0; j < 8; ++j)
-          if ((eq >> j) & 1u) { if (seen >= room) take &= ~(1u << j); ++seen; }
-        const uint32_t chosen = gt | take;
-        const int nch = __popc(chosen);
-        int cincl = nch;
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) {
-          const int t = __shfl_up_sync(0xffffffffu, cincl, o, 16);
-          if (sg >= o) cincl += t;
-        }
-        int slot = s_outb[rr] + cincl - nch;
-        const int t = t0 + rr;
-        if (t < p.T) {
-          int* out = p.idx + ((size_t)head * p.T + t) * p.kcap;
-          for (int j = 0; j < 8; ++j)
-            if ((chosen >> j) & 1u) {
-              if (slot < p.kcap) out[slot] = c0 + sg * 8 + j;
-              ++slot;
-            }
-        }
-        const int etot = __shfl_sync(0xffffffffu, eincl, (lane & 16) | 15);
-        const int ctot = __shfl_sync(0xffffffffu, cincl, (lane & 16) | 15);
-        __syncwarp();
-        if (sg == 15) { s_eqb[rr] += etot; s_outb[rr] += ctot; }
-        if (sg < 4) { m_gt[rr * 4 + sg] = 0; m_eq[rr * 4 + sg] = 0; }
-      }
-      __syncthreads();
-    }
-    if (sweep < 3) {
-      // one warp per row: pivot of this sweep's digit, then clear the row's histogram
-#pragma unroll 1
-      for (int rr = warp; rr < kPfRows; rr += kWarps) {
-        if (s_state[rr] != 1) continue;
-        const int nb = sweep == 2 ? 1024 : 2048;
-        uint32_t bin, above, in_bin;
-        pf_pivot(hist + rr * (kPfBins / 2), nb, s_need[rr], lane, bin, above, in_bin);
-        if (lane == 0) {
-          const uint32_t need = s_need[rr] - above;
-          s_pref[rr] = sweep == 0 ? bin : (sweep == 1 ? (s_pref[rr] << 11) | bin : (s_pref[rr] << 10) | bin);
-          s_shift[rr] = sweep == 0 ? 21 : (sweep == 1 ? 10 : 0);
-          s_need[rr] = need;
-          if (need == in_bin || sweep == 2) s_state[rr] = 2;
-        }
-        __syncwarp();
-        for (int i = lane; i < kPfBins / 2; i += 32) hist[rr * (kPfBins / 2) + i] = 0;
-      }
-      __syncthreads();
-    }
+  }
+  tmem_fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    tmem_fence_after_sync();
+    tmem_dealloc(tbase, kPfTmemCols);
   }
 }
 

@@ -186,9 +186,11 @@ def topk_indices(scores: np.ndarray, k: int) -> np.ndarray:
     if k <= 0:
         return np.zeros(scores.shape[:-1] + (0,), dtype=np.int64)
     s = np.asarray(scores, dtype=np.float64)
-    s = np.where(np.isnan(s), np.inf, s)
+    nan = np.isnan(s)
+    s = np.where(nan, 0.0, s)
     idx = np.broadcast_to(np.arange(s.shape[-1]), s.shape)
-    order = np.lexsort((idx, -s), axis=-1)          # last key is primary: -s ascending, then index ascending
+    # last key is primary: NaN first (above +inf), then -s ascending, then index ascending
+    order = np.lexsort((idx, -s, ~nan), axis=-1)
     return order[..., :k].astype(np.int64)
 
 

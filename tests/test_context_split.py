@@ -78,7 +78,8 @@ class OracleOps:
         for b in range(B):
             for g in range(G):
                 off = (b * G + g) * plan.shard_capacity
-                order = np.lexsort((pos, -np.where(np.isnan(s[b, g]), np.inf, s[b, g])))[:plan.k_local]
+                nan = np.isnan(s[b, g])
+                order = np.lexsort((pos, -np.where(nan, 0.0, s[b, g]), ~nan))[:plan.k_local]
                 chosen = np.sort(order)                                      # ascending position
                 k64 = (_order_key(s[b, g][chosen]) << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - pos[chosen].astype(np.uint64))
                 keys[b, g, :plan.k_local] = k64

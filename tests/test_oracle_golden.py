@@ -142,6 +142,9 @@ def test_topk_tie_rule_and_nan():
     assert orc.topk_indices(s, 3).tolist() == [[3, 1, 2]]
     assert orc.topk_indices(s, 4).tolist() == [[3, 1, 2, 5]]
     assert orc.topk_indices(s, 0).shape == (1, 0)
+    # NaN ranks above +inf (torch.topk's order), equal NaNs and equal infinities by position
+    s = np.array([[np.inf, 1.0, np.nan, np.inf, np.nan, -np.inf]])
+    assert orc.topk_indices(s, 6).tolist() == [[2, 4, 0, 3, 1, 5]]
 
 
 def test_context_split_protocol_equals_single_device():

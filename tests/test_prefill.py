@@ -53,10 +53,16 @@ def _check(u, zT, q_pos0, k, kcap, idx, scores):
         lay = orc.selection_layout(q_pos0 + t + 1)
         if lay.candidates == 0:
             continue
-        want = np.einsum("hj,hjc->hc", u64[:, t], z64[:, :, lay.lo:lay.hi])
-        bound = 32 * 2.0 ** -24 * np.einsum("hj,hjc->hc", np.abs(u64[:, t]), np.abs(z64[:, :, lay.lo:lay.hi])) + 1e-30
-        err = np.abs(s[:, t, lay.lo:lay.hi] - want)
-        assert (err <= bound).all(), f"row {t}: score error {err.max():.3e} above the fp32 bound"
+        with np.errstate(invalid="ignore", over="ignore"):
+            want = np.einsum("hj,hjc->hc", u64[:, t], z64[:, :, lay.lo:lay.hi])
+            bound = 32 * 2.0 ** -24 * np.einsum("hj,hjc->hc", np.abs(u64[:, t]), np.abs(z64[:, :, lay.lo:lay.hi])) + 1e-30
+        got = s[:, t, lay.lo:lay.hi]
+        fin = np.isfinite(want)
+        err = np.abs(got[fin] - want[fin])
+        assert (err <= bound[fin]).all(), f"row {t}: score error {err.max():.3e} above the fp32 bound"
+        assert (np.isnan(got[~fin]) == np.isnan(want[~fin])).all(), f"row {t}: NaN scores differ"
+        inf = ~fin & ~np.isnan(want)
+        assert (got[inf] == want[inf]).all(), f"row {t}: infinite scores differ"
     want = orc.prefill_topk(u64, z64, q_pos0, k, kcap, scores=s)
     got = idx.cpu().numpy()
     bad = np.argwhere((got != want).any(axis=-1))
@@ -84,6 +90,50 @@ def test_prefill_topk_matches_the_oracle(H, T, q_pos0, C, k, kcap, ties):
         for c in range(ties):
             col = s[:, -1, lay.lo + c:lay.hi:ties]
             assert (col == col[:, :1]).all(), "equal columns must score equally"
+    _check(u, zT, q_pos0, k, kcap, idx, scores)
+    again = ops.prefill_score_topk(u.to(DEV), zT.to(DEV), k, q_pos0=q_pos0, kcap=kcap)
+    assert torch.equal(idx, again), "the selection must not depend on the diagnostic scores output"
+
+
+def _shaped(H, T, C, seed, kind):
+    """Inputs that drive the scorer's less common paths: `neg` (most scores negative: thresholds below zero),
+    `outlier` (a few huge columns at the start of every row: the first histogram's window starts far too high),
+    `zero` (all-zero query rows: every score of those rows is 0), `nonfinite` (NaN and infinite scores)."""
+    g = torch.Generator().manual_seed(seed)
+    u = torch.randn(H, T, 32, generator=g)
+    zT = torch.randn(H, 32, C, generator=g)
+    if kind == "neg":
+        u = u.abs()
+        zT = -zT.abs() + 0.3 * torch.randn(H, 32, C, generator=g)
+    elif kind == "outlier":
+        zT[:, :, 4:12] *= 4096.0
+    elif kind == "zero":
+        u[:, ::3] = 0.0
+    elif kind == "nonfinite":
+        zT[:, :, 40:44] = float("inf")          # +-inf or NaN (0 * inf, inf - inf) depending on u
+        zT[:, 5, 300:302] = float("nan")
+        u[:, 7::50, 3] = float("inf")
+        u[:, 11::50] = float("nan")
+    return u.to(torch.bfloat16), zT.to(torch.bfloat16).contiguous()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,H,T,q_pos0,C,k,kcap", [
+    ("neg", 2, 700, 0, 1024, 256, 256),
+    ("outlier", 2, 500, 900, 1536, 128, 128),
+    ("zero", 1, 400, 300, 768, 256, 256),
+    ("nonfinite", 2, 600, 100, 1024, 200, 256),
+    ("plain", 1, 700, 600, 1408, 400, 450),        # k > 256: positions written straight to the output rows
+])
+def test_prefill_topk_uncommon_paths_match_the_oracle(kind, H, T, q_pos0, C, k, kcap):
+    from attention_lab_b200 import ops
+    if kind == "plain":
+        u, zT = _inputs(H, T, C, seed=3)
+    else:
+        u, zT = _shaped(H, T, C, seed=T + C, kind=kind)
+    scores = torch.full((H, T, C), float("nan"), dtype=torch.float32, device=DEV)
+    idx = ops.prefill_score_topk(u.to(DEV), zT.to(DEV), k, q_pos0=q_pos0, kcap=kcap, scores_out=scores)
+    torch.cuda.synchronize()
     _check(u, zT, q_pos0, k, kcap, idx, scores)
     again = ops.prefill_score_topk(u.to(DEV), zT.to(DEV), k, q_pos0=q_pos0, kcap=kcap)
     assert torch.equal(idx, again), "the selection must not depend on the diagnostic scores output"
