@@ -7,9 +7,9 @@
 // One CTA serves 128 query rows of one head: the tensor cores compute a 128 x 128 tile of scores per step
 // (tcgen05.mma, kind::f16, bf16 operands from shared memory, fp32 accumulators in tensor memory), zT tiles arrive by
 // TMA (128-byte swizzle, the layout the MMA reads as an N-major operand) in a 4-stage ring, and the accumulators sit in
-// two 128-column TMEM buffers so the next tile is multiplied while the current one is read. Four warps read TMEM with
-// one thread per query row (TMEM lane = row), so every row's keys pass through one thread in position order; a fifth
-// warp issues the copies and the MMAs. Scores are never stored: each sweep over the columns recomputes them (the MMA
+// two 128-column TMEM buffers so the next tile is multiplied while the current one is read. Eight warps read TMEM, two
+// threads per query row (TMEM lane = row): one takes columns 0-63 of every tile, the other 64-127; a ninth warp issues
+// the copies and the MMAs. Scores are never stored: each sweep over the columns recomputes them (the MMA
 // is deterministic, so every sweep sees the same values).
 //
 // Selection per row, on order-preserving integer keys of the scores:
@@ -18,7 +18,8 @@
 //                    holding the k-th largest key becomes the row's window.
 //   gather sweep:    the window's keys (at most 128) are copied to shared memory; one warp finds the exact k-th
 //                    largest among them (a bitwise select), and how many keys equal to it are still to be taken.
-//   emit sweep:      keys above the threshold, plus the first `need` keys equal to it, in position order.
+//   emit sweep:      keys above the threshold, plus the first `need` keys equal to it, in position order (the two
+//                    threads of a row swap their per-tile counts to place their positions).
 // A window holding more than 128 keys is split again by a finer histogram sweep (bins of 2^12, 2^5, 1 units). While
 // the row's scores are finite and the window lies above zero, the key of a score is its raw float bit pattern (an
 // order-preserving integer for positive floats); rows with a NaN or infinity, a non-positive anchor, or a window that
@@ -35,20 +36,20 @@ constexpr int kPfRows = 128;               // query rows per CTA: the MMA's M, o
 constexpr int kPfTile = 128;               // columns per tile: the MMA's N
 constexpr int kPfR = 32;                   // index dimension r: the MMA's K (two kind::f16 steps of 16)
 constexpr int kPfStages = 4;               // zT tiles in flight (even: stage reuse tracks the TMEM buffer's barrier)
-constexpr int kPfRowWarps = 4;             // warps reading TMEM, one thread per query row
+constexpr int kPfRowWarps = 8;             // warps reading TMEM: two per lane quarter, two threads per query row
 constexpr int kPfThreads = 32 * (kPfRowWarps + 1);
 constexpr int kPfBins = 128;
 constexpr int kPfFirstShift = 19;          // first histogram: bins of 2^19 key units
-constexpr int kPfGather = 128;             // keys gathered per row
+constexpr int kPfGather = 128;             // keys gathered per row (64 per thread of the row)
 constexpr int kPfStaged = 256;             // staged output positions per row (k <= 256)
 constexpr int kPfTmemCols = 2 * kPfTile;
 constexpr uint32_t kPfStageBytes = kPfR * kPfTile * 2;               // 8 KB: two 64-column boxes of 32 rows
 constexpr uint32_t kPfABytes = kPfRows * kPfR * 2;                   // 8 KB of u rows
-constexpr uint32_t kPfWorkBytes = kPfRows * kPfBins * 4;             // 64 KB: histogram / gather / staging
+constexpr uint32_t kPfWorkBytes = kPfRows * (kPfBins + 1) * 4;       // histogram (+ a sink bin) / gather / staging
 constexpr size_t kPfSmem = 1024 + kPfStages * kPfStageBytes + kPfABytes + kPfWorkBytes;
 
 static_assert(kPfStages % 2 == 0, "stage s is reused by the tile that reuses its TMEM buffer");
-static_assert(kPfGather * kPfRows * 4 == kPfWorkBytes && kPfStaged * kPfRows * 2 == kPfWorkBytes, "work area");
+static_assert(kPfGather * kPfRows * 4 <= kPfWorkBytes && kPfStaged * kPfRows * 2 <= kPfWorkBytes, "work area");
 
 // Row states (one thread per row).
 constexpr int kPfNone = 0, kPfHist = 1, kPfGatherSt = 2, kPfEmit = 3, kPfDone = 4;
@@ -164,49 +165,88 @@ __device__ __forceinline__ int pf_ld16(uint32_t saddr) {
   return (int)v;
 }
 
+// Per-thread pointers and roles of a row thread.
+struct PfCtx {
+  uint32_t tcol;        // TMEM address of the warp's lane quarter, column 0
+  uint32_t hist;        // the row's bin-0 word of the histogram (bins 512 bytes apart; bin kPfBins is a sink)
+  uint32_t gbuf;        // this thread's 64 gather slots (the row's 512-byte slot, second half for half 1)
+  uint32_t stage;       // the row's staged output positions (16-bit), the same 512-byte slot
+  int* out;             // the row's output positions (used directly when k > kPfStaged)
+  float* srow;          // the row's scores (optional)
+  int half;             // 0: columns 0-63 of every tile, 1: columns 64-127
+  int q;                // lane quarter (named barrier 2 + q pairs the row's two warps)
+  int row;
+  bool staged;
+};
 
-// One 32-column chunk of a row's scores v (columns c0 .. c0 + 31), of which [jlo, jhi) are candidates unless FULL.
-//   KIND kPfHist:     count each key of the window in the row's histogram (hist: this row's bin-0 word; bins are
-//                     512 bytes apart). FIRST: the row's first sweep (whole key range; fast mode adds up the scores).
-//   KIND kPfGatherSt: append the window's keys to the row's list (work: the row's 512-byte slot).
-//   KIND kPfEmit:     append the chosen positions (TIE: only the first eqleft keys equal to thr are taken) to the
-//                     row's staged list (16-bit, in work) or straight to its output row.
-// Key differences are taken in unsigned arithmetic (windows may span the whole signed range).
-template <int KIND, bool GEN, bool FULL, bool FIRST, bool TIE>
-__device__ __forceinline__ void pf_chunk(const uint32_t (&v)[32], int c0, int jlo, int jhi, PfRow& r, uint32_t hist,
-                                         uint32_t work, int* out, bool staged) {
+// Candidates [jlo, jhi) of a 32-column chunk as a bit mask (0 < jhi, jlo < 32).
+__device__ __forceinline__ uint32_t pf_vmask(int jlo, int jhi) {
+  const uint32_t hi = jhi >= 32 ? 0xffffffffu : ((1u << jhi) - 1u);
+  const uint32_t lo = jlo <= 0 ? 0xffffffffu : ~((1u << jlo) - 1u);
+  return hi & lo;
+}
+
+// Histogram sweep, one chunk: every key of the window adds one to its bin (top - min(key, top)) >> sh, capped at
+// 127; keys outside the window or outside the row's candidates go to the sink bin, so every key is one
+// unconditional shared-memory reduction. FIRST: the row's first sweep (its window is every key; fast-mode rows sum
+// their scores in four chains to detect a NaN or an infinity).
+template <bool GEN, bool FULL, bool FIRST>
+__device__ __forceinline__ void pf_hist_chunk(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t hist) {
+  float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    if (!FULL && (j < jlo || j >= jhi)) continue;
+    const bool valid = FULL || ((vm >> j) & 1u);
     const int key = GEN ? pf_canon(v[j]) : (int)v[j];
-    if (KIND == kPfHist) {
-      if (FIRST && !GEN) r.sum += __uint_as_float(v[j]);
-      if (!FIRST && (unsigned)key - (unsigned)r.wlo > (unsigned)r.whi - (unsigned)r.wlo) continue;
-      const unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> r.sh, (unsigned)(kPfBins - 1));
-      pf_red_add(hist + (d << 9));
-    } else if (KIND == kPfGatherSt) {
-      if ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) {
-        if (r.cnt < kPfGather) pf_st32(work + ((uint32_t)r.cnt << 2), key);
-        ++r.cnt;
-      }
-    } else {
-      bool take;
-      if (TIE) {
-        const bool eq = key == r.thr;
-        take = key > r.thr || (eq && r.eqleft > 0);
-        if (eq && take) --r.eqleft;
-      } else {
-        take = key >= r.thr;
-      }
-      if (take) {
-        if (r.cnt < r.kk) {                     // always, unless the launch was flagged invalid
-          if (staged) pf_st16(work + ((uint32_t)r.cnt << 1), c0 + j);
-          else out[r.cnt] = c0 + j;
-        }
-        ++r.cnt;
-      }
+    if (FIRST && !GEN) a[j & 3] += valid ? __uint_as_float(v[j]) : 0.0f;
+    unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> r.sh, (unsigned)(kPfBins - 1));
+    bool in = valid;
+    if (!FIRST) in = in && ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo);
+    if (!(FULL && FIRST)) d = in ? d : (unsigned)kPfBins;
+    pf_red_add(hist + (d << 9));
+  }
+  if (FIRST && !GEN) r.sum += (a[0] + a[1]) + (a[2] + a[3]);
+}
+
+// Gather sweep, one chunk: the window's keys go to this thread's slots (at most 64 are stored; more marks an
+// overflow, found after the sweep).
+template <bool GEN, bool FULL>
+__device__ __forceinline__ void pf_gather_chunk(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t gbuf) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const bool valid = FULL || ((vm >> j) & 1u);
+    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
+    if (valid && (unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) {
+      if (r.cnt < kPfGather / 2) pf_st32(gbuf + ((uint32_t)r.cnt << 2), key);
+      ++r.cnt;
     }
   }
+}
+
+// Emit sweep, one chunk: bit j of `take` for a key above the threshold (every key at or above it unless TIE), bit j
+// of `eq` for a key equal to it (TIE only), both limited to the candidates.
+template <bool GEN, bool TIE>
+__device__ __forceinline__ void pf_emit_chunk(const uint32_t (&v)[32], uint32_t vm, const PfRow& r, uint32_t& take,
+                                              uint32_t& eq) {
+  uint32_t t = 0, e = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
+    if (TIE) {
+      t |= (key > r.thr ? 1u : 0u) << j;
+      e |= (key == r.thr ? 1u : 0u) << j;
+    } else {
+      t |= (key >= r.thr ? 1u : 0u) << j;
+    }
+  }
+  take = t & vm;
+  eq = e & vm;
+}
+
+// The n lowest set bits of m.
+__device__ __forceinline__ uint32_t pf_keep_low(uint32_t m, int n) {
+  uint32_t o = 0;
+  while (n > 0 && m) { const uint32_t b = m & (0u - m); o |= b; m ^= b; --n; }
+  return o;
 }
 
 // The row's anchor, from the candidates of its first chunk: twice their largest score. A row without a positive
@@ -237,31 +277,53 @@ __device__ __forceinline__ void pf_wait(uint64_t* bar, unsigned parity, volatile
   }
 }
 
-template <int KIND, bool GEN, bool FULL, bool FIRST>
-__device__ __forceinline__ void pf_chunk_tie(const uint32_t (&v)[32], int c0, int jlo, int jhi, PfRow& r, uint32_t hist,
-                                             uint32_t work, int* out, bool staged) {
-  if (KIND == kPfEmit && r.tie) pf_chunk<KIND, GEN, FULL, FIRST, true>(v, c0, jlo, jhi, r, hist, work, out, staged);
-  else pf_chunk<KIND, GEN, FULL, FIRST, false>(v, c0, jlo, jhi, r, hist, work, out, staged);
-}
-
-template <int KIND, bool FIRST>
-__device__ __forceinline__ void pf_dispatch(const uint32_t (&v)[32], int c0, int jlo, int jhi, bool full, PfRow& r,
-                                            uint32_t hist, uint32_t work, int* out, bool staged) {
-  if (r.gen) {
-    if (full) pf_chunk_tie<KIND, true, true, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
-    else pf_chunk_tie<KIND, true, false, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
-  } else {
-    if (full) pf_chunk_tie<KIND, false, true, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
-    else pf_chunk_tie<KIND, false, false, FIRST>(v, c0, jlo, jhi, r, hist, work, out, staged);
+// Emit sweep, end of a tile: the two threads of the row swap their counts (keys above the threshold, keys equal to
+// it) through shared memory, the lower half takes its ties first, and each writes its positions in order after the
+// other's when it is the upper half. Both threads keep the same running count.
+__device__ __forceinline__ void pf_emit_tile(const PfCtx& c, PfRow& r, uint32_t* s_ex, int par, int cbase,
+                                             uint32_t (&take)[2], uint32_t (&eq)[2]) {
+  const uint32_t mine = (uint32_t)(__popc(take[0]) + __popc(take[1])) |
+                        ((uint32_t)(__popc(eq[0]) + __popc(eq[1])) << 16);
+  s_ex[(par * 2 + c.half) * kPfRows + c.row] = mine;
+  asm volatile("bar.sync %0, 64;\n" ::"r"(2 + c.q) : "memory");
+  const uint32_t xa = s_ex[(par * 2 + 0) * kPfRows + c.row], xb = s_ex[(par * 2 + 1) * kPfRows + c.row];
+  const int gta = (int)(xa & 0xffffu), eqa = (int)(xa >> 16), gtb = (int)(xb & 0xffffu), eqb = (int)(xb >> 16);
+  const int rem = r.eqleft > 0 ? r.eqleft : 0;
+  const int alla = min(eqa, rem), allb = min(eqb, rem - alla);
+  int allow = c.half ? allb : alla;
+  uint32_t m0 = take[0], m1 = take[1];
+  if (eq[0] | eq[1]) {
+    const uint32_t e0 = pf_keep_low(eq[0], allow);
+    allow -= __popc(e0);
+    m0 |= e0;
+    m1 |= pf_keep_low(eq[1], allow);
   }
+  int slot = r.cnt + (c.half ? gta + alla : 0);
+  const int cap = r.kk;
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    uint32_t m = w ? m1 : m0;
+    const int cb = cbase + 32 * w;
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      if (slot < cap) {                       // always, unless the launch was flagged invalid
+        if (c.staged) pf_st16(c.stage + ((uint32_t)slot << 1), cb + j);
+        else c.out[slot] = cb + j;
+      }
+      ++slot;
+    }
+  }
+  r.cnt += gta + alla + gtb + allb;
+  r.eqleft -= alla + allb;
 }
 
-// One sweep of a row thread over nt tiles of TMEM scores (global tile counter g). Rows in state KIND do that sweep's
-// work; in the CTA's first sweep every row with candidates also writes its scores when asked to.
+// One sweep of a row thread over nt tiles of TMEM scores (global tile counter g): this thread's two chunks of each
+// tile (columns 64 * half .. + 63). Rows in state KIND do that sweep's work; in the CTA's first sweep every row with
+// candidates also writes its scores when asked to.
 template <int KIND>
-__device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, uint32_t tcol, uint64_t* tfull, uint64_t* tfree,
-                         uint32_t hist, uint32_t work, int* out, float* srow, bool staged, volatile int* abort_flag,
-                         unsigned* err) {
+__device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, const PfCtx& c, uint64_t* tfull, uint64_t* tfree,
+                         uint32_t* s_ex, volatile int* abort_flag, unsigned* err) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int i = 0; i < nt; ++i, ++g) {
@@ -270,58 +332,77 @@ __device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, uint32_t tcol, ui
     tmem_fence_after_sync();
     const int c0 = i * kPfTile;
     const bool act = r.state == KIND;
-    const bool wscore = first && srow != nullptr && r.hi > r.lo;
-#pragma unroll 1
-    for (int q = 0; q < kPfTile / 32; ++q) {
+    if (KIND == kPfHist && first && i == 0) {          // the anchor: both threads of the row read chunk 0
       uint32_t v[32];
-      pf_tmem_ld32(tcol + (uint32_t)(buf * kPfTile + q * 32), v);
+      pf_tmem_ld32(c.tcol + (uint32_t)(buf * kPfTile), v);
       pf_tmem_wait(v);
-      if (q == kPfTile / 32 - 1) {             // the buffer is in registers: the MMA may overwrite it
+      if (act) pf_anchor(v, r.lo, r.hi, r);
+    }
+    uint32_t take[2] = {0u, 0u}, eq[2] = {0u, 0u};
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      const int cq = c0 + 64 * c.half + 32 * w;
+      uint32_t v[32];
+      pf_tmem_ld32(c.tcol + (uint32_t)(buf * kPfTile + 64 * c.half + 32 * w), v);
+      pf_tmem_wait(v);
+      if (w == 1) {                                     // the buffer is in registers: the MMA may overwrite it
         tmem_fence_before_sync();
         __syncwarp();
         if (lane == 0) pf_arrive(&tfree[buf]);
       }
-      const int cq = c0 + 32 * q;
-      const int jlo = r.lo - cq, jhi = r.hi - cq;       // candidates of this chunk: [jlo, jhi) clipped to [0, 32)
+      const int jlo = r.lo - cq, jhi = r.hi - cq;      // candidates of this chunk: [jlo, jhi) clipped to [0, 32)
       if (jhi <= 0 || jlo >= 32) continue;
       const bool full = jlo <= 0 && jhi >= 32;
-      if (wscore) {
+      const uint32_t vm = full ? 0xffffffffu : pf_vmask(jlo, jhi);
+      if (first && c.srow != nullptr) {
         if (full) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
-            *reinterpret_cast<float4*>(srow + cq + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                                    __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+            *reinterpret_cast<float4*>(c.srow + cq + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                      __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
         } else {
 #pragma unroll
           for (int j = 0; j < 32; ++j)
-            if (j >= jlo && j < jhi) srow[cq + j] = __uint_as_float(v[j]);
+            if ((vm >> j) & 1u) c.srow[cq + j] = __uint_as_float(v[j]);
         }
       }
       if (KIND == kPfNone || !act) continue;
-      if (KIND == kPfHist && first) {
-        if (i == 0 && q == 0) pf_anchor(v, jlo, jhi, r);
-        pf_dispatch<KIND, true>(v, cq, jlo, jhi, full, r, hist, work, out, staged);
-      } else {
-        pf_dispatch<KIND, false>(v, cq, jlo, jhi, full, r, hist, work, out, staged);
+      if (KIND == kPfHist) {
+        if (first) {
+          if (r.gen) { if (full) pf_hist_chunk<true, true, true>(v, vm, r, c.hist); else pf_hist_chunk<true, false, true>(v, vm, r, c.hist); }
+          else { if (full) pf_hist_chunk<false, true, true>(v, vm, r, c.hist); else pf_hist_chunk<false, false, true>(v, vm, r, c.hist); }
+        } else {
+          if (r.gen) pf_hist_chunk<true, false, false>(v, vm, r, c.hist);
+          else pf_hist_chunk<false, false, false>(v, vm, r, c.hist);
+        }
+      } else if (KIND == kPfGatherSt) {
+        if (r.gen) { if (full) pf_gather_chunk<true, true>(v, vm, r, c.gbuf); else pf_gather_chunk<true, false>(v, vm, r, c.gbuf); }
+        else { if (full) pf_gather_chunk<false, true>(v, vm, r, c.gbuf); else pf_gather_chunk<false, false>(v, vm, r, c.gbuf); }
+      } else if (KIND == kPfEmit) {
+        if (r.tie) {
+          if (r.gen) pf_emit_chunk<true, true>(v, vm, r, take[w], eq[w]); else pf_emit_chunk<false, true>(v, vm, r, take[w], eq[w]);
+        } else {
+          if (r.gen) pf_emit_chunk<true, false>(v, vm, r, take[w], eq[w]); else pf_emit_chunk<false, false>(v, vm, r, take[w], eq[w]);
+        }
       }
     }
+    if (KIND == kPfEmit) pf_emit_tile(c, r, s_ex, g & 1, c0 + 64 * c.half, take, eq);
   }
 }
 
-// After a histogram sweep: the bin holding the row's need-th largest key (counting from the top) becomes the window;
-// the row's 128 bins are cleared on the way. `first`: the row's first sweep, after which a fast-mode row whose scores
-// did not sum to a finite value (a NaN or an infinity among them) starts over with canonical keys.
-__device__ __forceinline__ void pf_after_hist(PfRow& r, uint32_t hist, bool first) {
+// After a histogram sweep (both threads of the row, reading the same counts): the bin holding the row's need-th
+// largest key (counting from the top) becomes the window. `bad`: after the row's first sweep, a fast-mode row whose
+// scores did not sum to a finite value (a NaN or an infinity among them) starts over with canonical keys.
+__device__ __forceinline__ void pf_after_hist(PfRow& r, uint32_t hist, bool bad) {
   unsigned cum = 0, before = 0, inb = 0;
   int piv = -1;
 #pragma unroll 8
   for (int d = 0; d < kPfBins; ++d) {
-    const unsigned c = pf_ld32(hist + ((uint32_t)d << 9));
-    pf_st32(hist + ((uint32_t)d << 9), 0);
-    if (piv < 0 && cum + c >= (unsigned)r.need) { piv = d; before = cum; inb = c; }
-    cum += c;
+    const unsigned cnt = pf_ld32(hist + ((uint32_t)d << 9));
+    if (piv < 0 && cum + cnt >= (unsigned)r.need) { piv = d; before = cum; inb = cnt; }
+    cum += cnt;
   }
-  if (first && !r.gen && !isfinite(r.sum)) { pf_restart_canonical(r); return; }
+  if (bad && !r.gen) { pf_restart_canonical(r); return; }
   if (piv < 0) { piv = kPfBins - 1; before = cum; inb = 0; }   // unreachable: the window holds the need-th key
   const long long top = r.top;
   long long hk = piv == 0 ? (long long)r.whi : top - ((long long)piv << r.sh);
@@ -341,64 +422,76 @@ __device__ __forceinline__ void pf_after_hist(PfRow& r, uint32_t hist, bool firs
   }
 }
 
-// After a gather sweep, one warp per row of its 32: the exact need-th largest of the gathered keys (an MSB-first
-// bitwise select on the offsets whi - key), the threshold and how many keys equal to it the row still takes.
-__device__ __forceinline__ void pf_after_gather(PfRow& r, uint32_t work_warp) {
+// A window whose keys overflowed a thread's gather slots: split it by a finer histogram instead.
+__device__ __forceinline__ void pf_refine(PfRow& r) {
+  const unsigned long long span = (unsigned long long)((long long)r.whi - (long long)r.wlo);
+  const int bits = 64 - __clzll((long long)span);
+  r.state = kPfHist; r.top = r.whi; r.sh = bits > 7 ? bits - 7 : 0;
+}
+
+// After a gather sweep, one warp per row of 16 (rows 32 q + 16 half .. + 15): the exact need-th largest of the
+// gathered keys (an MSB-first bitwise select on the offsets whi - key), then the threshold, how many keys equal to it
+// the row takes and whether that is fewer than all of them; an overflowed row is marked.
+__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const uint8_t* s_gc,
+                                           int* s_thr, int* s_eql, uint8_t* s_flag) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
-  for (int rr = 0; rr < 32; ++rr) {
-    if (__shfl_sync(0xffffffffu, r.state, rr) != kPfGatherSt) continue;
-    const int n = __shfl_sync(0xffffffffu, r.cnt, rr);
-    const int need = __shfl_sync(0xffffffffu, r.need, rr);
-    const int whi = __shfl_sync(0xffffffffu, r.whi, rr);
-    const int wlo = __shfl_sync(0xffffffffu, r.wlo, rr);
-    const uint32_t row = work_warp + (uint32_t)rr * (kPfGather * 4);
-    unsigned o[kPfGather / 32];
-    bool ok[kPfGather / 32];
+  for (int rr = 0; rr < 16; ++rr) {
+    const int ln = 16 * c.half + rr, row = 32 * c.q + ln;
+    if (__shfl_sync(0xffffffffu, r.state, ln) != kPfGatherSt) continue;
+    const int n0 = s_gc[row], n1 = s_gc[kPfRows + row];
+    if (n0 > kPfGather / 2 || n1 > kPfGather / 2) { if (lane == 0) s_flag[row] = 2; continue; }
+    const int need = __shfl_sync(0xffffffffu, r.need, ln);
+    const int whi = __shfl_sync(0xffffffffu, r.whi, ln);
+    const int wlo = __shfl_sync(0xffffffffu, r.wlo, ln);
+    const uint32_t slot = s_work + (uint32_t)row * (kPfGather * 4);
+    unsigned o[4];
+    bool ok[4];
 #pragma unroll
-    for (int q = 0; q < kPfGather / 32; ++q) {
-      const int i = lane + 32 * q;
-      ok[q] = i < n;
-      o[q] = ok[q] ? (unsigned)whi - pf_ld32(row + (uint32_t)i * 4) : 0u;
+    for (int qq = 0; qq < 4; ++qq) {
+      const int h = qq >> 1, i = lane + 32 * (qq & 1);
+      ok[qq] = i < (h ? n1 : n0);
+      o[qq] = ok[qq] ? (unsigned)whi - pf_ld32(slot + (uint32_t)h * (kPfGather * 2) + (uint32_t)i * 4) : 0u;
     }
     const unsigned span = (unsigned)whi - (unsigned)wlo;
     unsigned pref = 0;
     int rem = need;
 #pragma unroll 1
     for (int bit = 31 - __clz((int)(span | 1u)); bit >= 0; --bit) {
-      int c = 0;
+      int cnt = 0;
 #pragma unroll
-      for (int q = 0; q < kPfGather / 32; ++q) c += (ok[q] && ((o[q] ^ pref) >> bit) == 0u) ? 1 : 0;
-      c = (int)__reduce_add_sync(0xffffffffu, (unsigned)c);
-      if (c < rem) { rem -= c; pref |= 1u << bit; }
+      for (int qq = 0; qq < 4; ++qq) cnt += (ok[qq] && ((o[qq] ^ pref) >> bit) == 0u) ? 1 : 0;
+      cnt = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
+      if (cnt < rem) { rem -= cnt; pref |= 1u << bit; }
     }
     int gt = 0, eq = 0;
 #pragma unroll
-    for (int q = 0; q < kPfGather / 32; ++q) {
-      gt += (ok[q] && o[q] < pref) ? 1 : 0;
-      eq += (ok[q] && o[q] == pref) ? 1 : 0;
+    for (int qq = 0; qq < 4; ++qq) {
+      gt += (ok[qq] && o[qq] < pref) ? 1 : 0;
+      eq += (ok[qq] && o[qq] == pref) ? 1 : 0;
     }
     gt = (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);
     eq = (int)__reduce_add_sync(0xffffffffu, (unsigned)eq);
-    if (lane == rr) {
-      r.state = kPfEmit;
-      r.thr = (int)((unsigned)whi - pref);
-      r.eqleft = need - gt;
-      r.tie = r.eqleft < eq;
-      r.cnt = 0;
+    if (lane == 0) {
+      s_thr[row] = (int)((unsigned)whi - pref);
+      s_eql[row] = need - gt;
+      s_flag[row] = (need - gt) < eq ? 1 : 0;
     }
   }
 }
 
-
-// Grid (H, ceil(T / 128)), 160 threads: warps 0-3 hold one query row per thread, warp 4 issues TMA copies and MMAs.
+// Grid (H, ceil(T / 128)), 288 threads: warps 0-7 hold two threads per query row (warp w: lane quarter w % 4, column
+// half w / 4), warp 8 issues the TMA copies and the MMAs.
 __global__ void __launch_bounds__(kPfThreads, 2)
     prefill_topk_kernel(const PrefillParams p, const __grid_constant__ CUtensorMap zmap) {
   extern __shared__ __align__(1024) unsigned char pf_raw[];
   __shared__ uint64_t s_full[kPfStages], s_tfull[2], s_tfree[2];
   __shared__ uint32_t s_taddr;
-  __shared__ int s_nt, s_kind, s_flags, s_maxhi[4];
+  __shared__ int s_nt, s_kind, s_flags, s_maxhi[4], s_anyovf;
   __shared__ volatile int s_abort;
+  __shared__ uint32_t s_ex[2 * 2 * kPfRows];          // emit: [tile parity][half][row] counts
+  __shared__ int s_thr[kPfRows], s_eql[kPfRows];
+  __shared__ uint8_t s_gc[2 * kPfRows], s_flag[kPfRows], s_bad[kPfRows];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int head = blockIdx.x;
@@ -408,35 +501,40 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   const uint32_t s_stage = sb;
   const uint32_t s_a = sb + kPfStages * kPfStageBytes;
   const uint32_t s_work = s_a + kPfABytes;
+  const bool row_thread = warp < kPfRowWarps;
 
   if (tid == 0) {
     for (int s = 0; s < kPfStages; ++s) mbar_init(&s_full[s], 1);
     for (int b = 0; b < 2; ++b) { mbar_init(&s_tfull[b], 1); mbar_init(&s_tfree[b], kPfRowWarps); }
     mbar_init_fence();
-    s_abort = 0; s_flags = 0;
+    s_abort = 0; s_flags = 0; s_anyovf = 0;
     for (int i = 0; i < 4; ++i) s_maxhi[i] = 0;
   }
   if (warp == 0) { tmem_alloc(&s_taddr, kPfTmemCols); tmem_relinquish(); }
 
+  PfCtx c;
+  c.q = warp & 3; c.half = (warp >> 2) & 1; c.row = 32 * c.q + lane;
+  const int t = t0 + c.row;
   PfRow r;
   r.lo = 0; r.hi = 0; r.kk = 0; r.state = kPfNone; r.gen = false; r.need = 0; r.top = INT_MAX; r.sh = 25;
   r.wlo = INT_MIN; r.whi = INT_MAX; r.thr = INT_MIN; r.eqleft = 0; r.tie = false; r.cnt = 0; r.sum = 0.0f;
-  const int t = t0 + tid;
-  const bool row_thread = warp < kPfRowWarps;
   if (row_thread) {
-    // u row -> the MMA's A operand: K-major, no swizzle: 8 x (8 bf16) core matrices, K chunks 128 B apart, 8-row
-    // groups 512 B apart. Rows past the chunk are zero.
+    if (c.half == 0) {
+      // u row -> the MMA's A operand: K-major, no swizzle: 8 x (8 bf16) core matrices, K chunks 128 B apart, 8-row
+      // groups 512 B apart. Rows past the chunk are zero.
 #pragma unroll
-    for (int kc = 0; kc < kPfR / 8; ++kc) {
-      uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
-      if (t < p.T) {
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(p.u + (size_t)head * p.u_sh + (size_t)t * p.u_st + kc * 8);
-        w0 = src[0]; w1 = src[1]; w2 = src[2]; w3 = src[3];
+      for (int kc = 0; kc < kPfR / 8; ++kc) {
+        uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+        if (t < p.T) {
+          const uint32_t* src = reinterpret_cast<const uint32_t*>(p.u + (size_t)head * p.u_sh + (size_t)t * p.u_st + kc * 8);
+          w0 = src[0]; w1 = src[1]; w2 = src[2]; w3 = src[3];
+        }
+        const uint32_t dst = s_a + (uint32_t)(c.row >> 3) * 512u + (uint32_t)kc * 128u + (uint32_t)(c.row & 7) * 16u;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
       }
-      const uint32_t dst = s_a + (uint32_t)(tid >> 3) * 512u + (uint32_t)kc * 128u + (uint32_t)(tid & 7) * 16u;
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
+      s_bad[c.row] = 0; s_flag[c.row] = 0;
     }
-    for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += kPfRows * 16u)
+    for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += 2 * kPfRows * 16u)
       asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};\n" ::"r"(s_work + o), "r"(0) : "memory");
     if (t < p.T) {
       const int L = p.q_pos0 + t + 1;
@@ -454,12 +552,13 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   tmem_fence_after_sync();
   const uint32_t tbase = s_taddr;
 
-  const bool staged = p.k <= kPfStaged;
-  const uint32_t hist = s_work + (uint32_t)tid * 4u;                         // bin d of this row: + d * 512
-  const uint32_t work = s_work + (uint32_t)tid * (kPfGather * 4);            // this row's gather / staging slot
-  int* out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
-  float* srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
-  const uint32_t tcol = tbase + ((uint32_t)(32 * (warp & 3)) << 16);
+  c.staged = p.k <= kPfStaged;
+  c.tcol = tbase + ((uint32_t)(32 * c.q) << 16);
+  c.hist = s_work + (uint32_t)c.row * 4u;
+  c.stage = s_work + (uint32_t)c.row * (kPfGather * 4);
+  c.gbuf = c.stage + (uint32_t)c.half * (kPfGather * 2);
+  c.out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
+  c.srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
   const uint64_t adesc0 = pf_sdesc(s_a, 128, 512, 0);
 
   int g = 0;
@@ -480,7 +579,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         atomicMax(&s_maxhi[0], mh1); atomicMax(&s_maxhi[1], mh2); atomicMax(&s_maxhi[2], mh4);
         atomicMax(&s_maxhi[3], mha);
       }
-      asm volatile("bar.sync 1, %0;\n" ::"n"(kPfRows) : "memory");
+      asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
       if (tid == 0) {
         const int f = s_flags;
         const int kind = (f & 1) ? kPfHist : (f & 2) ? kPfGatherSt : (f & 4) ? kPfEmit : kPfNone;
@@ -533,23 +632,40 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       __syncwarp();
       g += nt;
     } else {
-      switch (kind) {
-        case kPfHist:
-          pf_sweep<kPfHist>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
-          if (r.state == kPfHist) pf_after_hist(r, hist, first);
-          break;
-        case kPfGatherSt:
-          pf_sweep<kPfGatherSt>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
-          __syncwarp();
-          pf_after_gather(r, s_work + (uint32_t)(32 * warp) * (kPfGather * 4));
-          break;
-        case kPfEmit:
-          pf_sweep<kPfEmit>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
-          if (r.state == kPfEmit) r.state = kPfDone;
-          break;
-        default:
-          pf_sweep<kPfNone>(nt, g, first, r, tcol, s_tfull, s_tfree, hist, work, out, srow, staged, &s_abort, p.err);
-          break;
+      if (kind == kPfHist) {
+        pf_sweep<kPfHist>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
+        if (first && r.state == kPfHist && !r.gen && !isfinite(r.sum)) s_bad[c.row] = 1;
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
+        const bool was = r.state == kPfHist;
+        if (was) pf_after_hist(r, c.hist, first && s_bad[c.row]);
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
+        if (was)                                         // clear the row's bins (and its sink) for the next histogram
+          for (int d = c.half * 65; d < min(kPfBins + 1, c.half * 65 + 65); ++d) pf_st32(c.hist + ((uint32_t)d << 9), 0);
+      } else if (kind == kPfGatherSt) {
+        pf_sweep<kPfGatherSt>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
+        s_gc[c.half * kPfRows + c.row] = (uint8_t)min(r.cnt, 255);
+        if (tid == 0) s_anyovf = 0;
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
+        pf_resolve(r, c, s_work, s_gc, s_thr, s_eql, s_flag);
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
+        if (r.state == kPfGatherSt) {
+          const int f = s_flag[c.row];
+          if (f == 2) {
+            pf_refine(r);
+            s_anyovf = 1;
+          } else {
+            r.state = kPfEmit; r.thr = s_thr[c.row]; r.eqleft = s_eql[c.row]; r.tie = f == 1; r.cnt = 0;
+          }
+        }
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
+        if (s_anyovf)                                    // a finer histogram follows: clear the work area
+          for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += 2 * kPfRows * 16u)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};\n" ::"r"(s_work + o), "r"(0) : "memory");
+      } else if (kind == kPfEmit) {
+        pf_sweep<kPfEmit>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
+        if (r.state == kPfEmit) r.state = kPfDone;
+      } else {
+        pf_sweep<kPfNone>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
       }
     }
     first = false;
@@ -561,19 +677,19 @@ __global__ void __launch_bounds__(kPfThreads, 2)
     for (int gg = max(0, g - kPfStages); gg < g; ++gg) mbar_wait(&s_full[gg % kPfStages], (unsigned)(gg / kPfStages) & 1u);
     mbar_wait(&s_tfull[(g - 1) & 1], (unsigned)((g - 1) >> 1) & 1u);
   }
-  // output rows: the staged positions (or the ones already written), then -1 up to kcap
+  // output rows (warp w: rows 32 q + 16 half .. + 15): the staged positions (or the ones already written), then -1
   if (row_thread) {
-    __syncwarp();
+    asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
     const int n_mine = (r.state == kPfDone) ? min(r.cnt, r.kk) : 0;
 #pragma unroll 1
-    for (int rr = 0; rr < 32; ++rr) {
-      const int tr = t0 + 32 * warp + rr;
-      const int n = __shfl_sync(0xffffffffu, n_mine, rr);
+    for (int rr = 0; rr < 16; ++rr) {
+      const int ln = 16 * c.half + rr, row = 32 * c.q + ln, tr = t0 + row;
+      const int n = __shfl_sync(0xffffffffu, n_mine, ln);
       if (tr >= p.T) continue;
       int* o = p.idx + ((size_t)head * p.T + tr) * p.kcap;
-      const uint32_t row = s_work + (uint32_t)(32 * warp + rr) * (kPfGather * 4);
-      if (staged) {
-        for (int j = lane; j < p.kcap; j += 32) o[j] = j < n ? pf_ld16(row + (uint32_t)j * 2) : -1;
+      const uint32_t st = s_work + (uint32_t)row * (kPfGather * 4);
+      if (c.staged) {
+        for (int j = lane; j < p.kcap; j += 32) o[j] = j < n ? pf_ld16(st + (uint32_t)j * 2) : -1;
       } else {
         for (int j = n + lane; j < p.kcap; j += 32) o[j] = -1;
       }
