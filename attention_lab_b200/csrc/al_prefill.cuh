@@ -13,8 +13,8 @@
 // is deterministic, so every sweep sees the same values).
 //
 // Selection per row, on order-preserving integer keys of the scores:
-//   histogram sweep: 128 bins of 2^19 key units (1/16 of an octave) below an anchor taken from the row's first 32
-//                    candidates (twice their maximum), keys above it in bin 0, below the window in bin 127. The bin
+//   histogram sweep: 128 bins of 2^19 key units (1/16 of an octave) below an anchor taken from the row's candidates
+//                    in the first tile (twice their maximum), keys above it in bin 0, below the window in bin 127. The bin
 //                    holding the k-th largest key becomes the row's window.
 //   gather sweep:    the window's keys (at most 128) are copied to shared memory; one warp finds the exact k-th
 //                    largest among them (a bitwise select), and how many keys equal to it are still to be taken.
@@ -169,8 +169,8 @@ __device__ __forceinline__ int pf_ld16(uint32_t saddr) {
 struct PfCtx {
   uint32_t tcol;        // TMEM address of the warp's lane quarter, column 0
   uint32_t hist;        // the row's bin-0 word of the histogram (bins 512 bytes apart; bin kPfBins is a sink)
-  uint32_t gbuf;        // this thread's 64 gather slots (the row's 512-byte slot, second half for half 1)
-  uint32_t stage;       // the row's staged output positions (16-bit), the same 512-byte slot
+  uint32_t stage;       // the row's 512-byte slot: 128 gathered keys, later 256 staged output positions (16-bit)
+  int* gcnt;            // the row's gathered-key count (shared by its two threads)
   int* out;             // the row's output positions (used directly when k > kPfStaged)
   float* srow;          // the row's scores (optional)
   int half;             // 0: columns 0-63 of every tile, 1: columns 64-127
@@ -207,17 +207,18 @@ __device__ __forceinline__ void pf_hist_chunk(const uint32_t (&v)[32], uint32_t 
   if (FIRST && !GEN) r.sum += (a[0] + a[1]) + (a[2] + a[3]);
 }
 
-// Gather sweep, one chunk: the window's keys go to this thread's slots (at most 64 are stored; more marks an
-// overflow, found after the sweep).
+// Gather sweep, one chunk: the window's keys go to the row's slots, placed by a counter the row's two threads share
+// (the window holds at most 128 keys; a larger count is caught after the sweep).
 template <bool GEN, bool FULL>
-__device__ __forceinline__ void pf_gather_chunk(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t gbuf) {
+__device__ __forceinline__ void pf_gather_chunk(const uint32_t (&v)[32], uint32_t vm, const PfRow& r, uint32_t slots,
+                                                int* gcnt) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
     const bool valid = FULL || ((vm >> j) & 1u);
     const int key = GEN ? pf_canon(v[j]) : (int)v[j];
     if (valid && (unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) {
-      if (r.cnt < kPfGather / 2) pf_st32(gbuf + ((uint32_t)r.cnt << 2), key);
-      ++r.cnt;
+      const int at = atomicAdd(gcnt, 1);
+      if (at < kPfGather) pf_st32(slots + ((uint32_t)at << 2), key);
     }
   }
 }
@@ -249,13 +250,18 @@ __device__ __forceinline__ uint32_t pf_keep_low(uint32_t m, int n) {
   return o;
 }
 
-// The row's anchor, from the candidates of its first chunk: twice their largest score. A row without a positive
-// finite maximum there uses canonical keys from the start.
-__device__ __forceinline__ void pf_anchor(const uint32_t (&v)[32], int jlo, int jhi, PfRow& r) {
+// Largest candidate score of a chunk (candidates [jlo, jhi)), NaN ignored.
+__device__ __forceinline__ float pf_chunk_max(const uint32_t (&v)[32], int jlo, int jhi) {
   float m = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 32; ++j)
     if (j >= jlo && j < jhi) m = fmaxf(m, __uint_as_float(v[j]));
+  return m;
+}
+
+// The row's anchor, from the largest score m among its candidates in the first tile: twice that. A row without a
+// positive finite maximum there uses canonical keys from the start.
+__device__ __forceinline__ void pf_anchor(float m, PfRow& r) {
   if (m > 0.0f && m <= 3.402823466e38f) {
     r.gen = false;
     r.top = __float_as_int(2.0f * m);
@@ -332,11 +338,16 @@ __device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, const PfCtx& c, u
     tmem_fence_after_sync();
     const int c0 = i * kPfTile;
     const bool act = r.state == KIND;
-    if (KIND == kPfHist && first && i == 0) {          // the anchor: both threads of the row read chunk 0
-      uint32_t v[32];
-      pf_tmem_ld32(c.tcol + (uint32_t)(buf * kPfTile), v);
-      pf_tmem_wait(v);
-      if (act) pf_anchor(v, r.lo, r.hi, r);
+    if (KIND == kPfHist && first && i == 0) {          // the anchor: both threads of the row read the whole tile
+      float m = -INFINITY;
+#pragma unroll 1
+      for (int w = 0; w < kPfTile / 32; ++w) {
+        uint32_t v[32];
+        pf_tmem_ld32(c.tcol + (uint32_t)(buf * kPfTile + 32 * w), v);
+        pf_tmem_wait(v);
+        m = fmaxf(m, pf_chunk_max(v, r.lo - 32 * w, r.hi - 32 * w));
+      }
+      if (act) pf_anchor(m, r);
     }
     uint32_t take[2] = {0u, 0u}, eq[2] = {0u, 0u};
 #pragma unroll
@@ -376,8 +387,8 @@ __device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, const PfCtx& c, u
           else pf_hist_chunk<false, false, false>(v, vm, r, c.hist);
         }
       } else if (KIND == kPfGatherSt) {
-        if (r.gen) { if (full) pf_gather_chunk<true, true>(v, vm, r, c.gbuf); else pf_gather_chunk<true, false>(v, vm, r, c.gbuf); }
-        else { if (full) pf_gather_chunk<false, true>(v, vm, r, c.gbuf); else pf_gather_chunk<false, false>(v, vm, r, c.gbuf); }
+        if (r.gen) { if (full) pf_gather_chunk<true, true>(v, vm, r, c.stage, c.gcnt); else pf_gather_chunk<true, false>(v, vm, r, c.stage, c.gcnt); }
+        else { if (full) pf_gather_chunk<false, true>(v, vm, r, c.stage, c.gcnt); else pf_gather_chunk<false, false>(v, vm, r, c.stage, c.gcnt); }
       } else if (KIND == kPfEmit) {
         if (r.tie) {
           if (r.gen) pf_emit_chunk<true, true>(v, vm, r, take[w], eq[w]); else pf_emit_chunk<false, true>(v, vm, r, take[w], eq[w]);
@@ -432,15 +443,15 @@ __device__ __forceinline__ void pf_refine(PfRow& r) {
 // After a gather sweep, one warp per row of 16 (rows 32 q + 16 half .. + 15): the exact need-th largest of the
 // gathered keys (an MSB-first bitwise select on the offsets whi - key), then the threshold, how many keys equal to it
 // the row takes and whether that is fewer than all of them; an overflowed row is marked.
-__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const uint8_t* s_gc,
+__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const int* s_gcnt,
                                            int* s_thr, int* s_eql, uint8_t* s_flag) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int rr = 0; rr < 16; ++rr) {
     const int ln = 16 * c.half + rr, row = 32 * c.q + ln;
     if (__shfl_sync(0xffffffffu, r.state, ln) != kPfGatherSt) continue;
-    const int n0 = s_gc[row], n1 = s_gc[kPfRows + row];
-    if (n0 > kPfGather / 2 || n1 > kPfGather / 2) { if (lane == 0) s_flag[row] = 2; continue; }
+    const int n = s_gcnt[row];
+    if (n > kPfGather) { if (lane == 0) s_flag[row] = 2; continue; }
     const int need = __shfl_sync(0xffffffffu, r.need, ln);
     const int whi = __shfl_sync(0xffffffffu, r.whi, ln);
     const int wlo = __shfl_sync(0xffffffffu, r.wlo, ln);
@@ -449,9 +460,9 @@ __device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint3
     bool ok[4];
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) {
-      const int h = qq >> 1, i = lane + 32 * (qq & 1);
-      ok[qq] = i < (h ? n1 : n0);
-      o[qq] = ok[qq] ? (unsigned)whi - pf_ld32(slot + (uint32_t)h * (kPfGather * 2) + (uint32_t)i * 4) : 0u;
+      const int i = lane + 32 * qq;
+      ok[qq] = i < n;
+      o[qq] = ok[qq] ? (unsigned)whi - pf_ld32(slot + (uint32_t)i * 4) : 0u;
     }
     const unsigned span = (unsigned)whi - (unsigned)wlo;
     unsigned pref = 0;
@@ -491,7 +502,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   __shared__ volatile int s_abort;
   __shared__ uint32_t s_ex[2 * 2 * kPfRows];          // emit: [tile parity][half][row] counts
   __shared__ int s_thr[kPfRows], s_eql[kPfRows];
-  __shared__ uint8_t s_gc[2 * kPfRows], s_flag[kPfRows], s_bad[kPfRows];
+  __shared__ int s_gcnt[kPfRows];
+  __shared__ uint8_t s_flag[kPfRows], s_bad[kPfRows];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int head = blockIdx.x;
@@ -532,7 +544,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         const uint32_t dst = s_a + (uint32_t)(c.row >> 3) * 512u + (uint32_t)kc * 128u + (uint32_t)(c.row & 7) * 16u;
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
       }
-      s_bad[c.row] = 0; s_flag[c.row] = 0;
+      s_bad[c.row] = 0; s_flag[c.row] = 0; s_gcnt[c.row] = 0;
     }
     for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += 2 * kPfRows * 16u)
       asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};\n" ::"r"(s_work + o), "r"(0) : "memory");
@@ -556,7 +568,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   c.tcol = tbase + ((uint32_t)(32 * c.q) << 16);
   c.hist = s_work + (uint32_t)c.row * 4u;
   c.stage = s_work + (uint32_t)c.row * (kPfGather * 4);
-  c.gbuf = c.stage + (uint32_t)c.half * (kPfGather * 2);
+  c.gcnt = &s_gcnt[c.row];
   c.out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
   c.srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
   const uint64_t adesc0 = pf_sdesc(s_a, 128, 512, 0);
@@ -641,12 +653,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
         if (was)                                         // clear the row's bins (and its sink) for the next histogram
           for (int d = c.half * 65; d < min(kPfBins + 1, c.half * 65 + 65); ++d) pf_st32(c.hist + ((uint32_t)d << 9), 0);
+        if (c.half == 0) s_gcnt[c.row] = 0;
       } else if (kind == kPfGatherSt) {
         pf_sweep<kPfGatherSt>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
-        s_gc[c.half * kPfRows + c.row] = (uint8_t)min(r.cnt, 255);
         if (tid == 0) s_anyovf = 0;
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
-        pf_resolve(r, c, s_work, s_gc, s_thr, s_eql, s_flag);
+        pf_resolve(r, c, s_work, s_gcnt, s_thr, s_eql, s_flag);
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
         if (r.state == kPfGatherSt) {
           const int f = s_flag[c.row];
