@@ -40,7 +40,7 @@ constexpr int kPfRowWarps = 8;             // warps reading TMEM: two per lane q
 constexpr int kPfThreads = 32 * (kPfRowWarps + 1);
 constexpr int kPfBins = 128;
 constexpr int kPfFirstShift = 19;          // first histogram: bins of 2^19 key units
-constexpr int kPfGather = 128;             // keys gathered per row (64 per thread of the row)
+constexpr int kPfGather = 128;             // keys gathered per row
 constexpr int kPfStaged = 256;             // staged output positions per row (k <= 256)
 constexpr int kPfTmemCols = 2 * kPfTile;
 constexpr uint32_t kPfStageBytes = kPfR * kPfTile * 2;               // 8 KB: two 64-column boxes of 32 rows
@@ -170,7 +170,8 @@ struct PfCtx {
   uint32_t tcol;        // TMEM address of the warp's lane quarter, column 0
   uint32_t hist;        // the row's bin-0 word of the histogram (bins 512 bytes apart; bin kPfBins is a sink)
   uint32_t stage;       // the row's 512-byte slot: 128 gathered keys, later 256 staged output positions (16-bit)
-  int* gcnt;            // the row's gathered-key count (shared by its two threads)
+  uint32_t gbase;       // this thread's first gather slot (half 0: slot 0, half 1: slot 127)
+  int gstep;            // +4 or -4 bytes per gathered key
   int* out;             // the row's output positions (used directly when k > kPfStaged)
   float* srow;          // the row's scores (optional)
   int half;             // 0: columns 0-63 of every tile, 1: columns 64-127
@@ -186,58 +187,80 @@ __device__ __forceinline__ uint32_t pf_vmask(int jlo, int jhi) {
   return hi & lo;
 }
 
-// Histogram sweep, one chunk: every key of the window adds one to its bin (top - min(key, top)) >> sh, capped at
-// 127; keys outside the window or outside the row's candidates go to the sink bin, so every key is one
-// unconditional shared-memory reduction. FIRST: the row's first sweep (its window is every key; fast-mode rows sum
-// their scores in four chains to detect a NaN or an infinity).
-template <bool GEN, bool FULL, bool FIRST>
-__device__ __forceinline__ void pf_hist_chunk(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t hist) {
+// Each sweep has one hot chunk routine (fast-mode keys, all 32 columns candidates, no ties) and one generic routine
+// (canonical keys where the row uses them, a candidate mask, ties), so the code that runs per key stays small.
+__device__ __forceinline__ int pf_key(uint32_t v, bool gen) { return gen ? pf_canon(v) : (int)v; }
+
+// Predicated shared store (no branch around it).
+__device__ __forceinline__ void pf_st32_if(uint32_t saddr, int v, bool p) {
+  asm volatile("{\n .reg .pred q;\n setp.ne.b32 q, %2, 0;\n @q st.shared.b32 [%0], %1;\n}\n"
+               ::"r"(saddr), "r"(v), "r"((int)p) : "memory");
+}
+
+// Histogram sweep, hot chunk (the row's first sweep in fast mode): every key adds one to its bin
+// (top - min(key, top)) >> 19, capped at 127, one unconditional shared-memory reduction per key; the scores are summed
+// in four chains to detect a NaN or an infinity.
+__device__ __forceinline__ void pf_hist_hot(const uint32_t (&v)[32], PfRow& r, uint32_t hist) {
   float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const bool valid = FULL || ((vm >> j) & 1u);
-    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
-    if (FIRST && !GEN) a[j & 3] += valid ? __uint_as_float(v[j]) : 0.0f;
-    unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> r.sh, (unsigned)(kPfBins - 1));
-    bool in = valid;
-    if (!FIRST) in = in && ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo);
-    if (!(FULL && FIRST)) d = in ? d : (unsigned)kPfBins;
+    const int key = (int)v[j];
+    a[j & 3] += __uint_as_float(v[j]);
+    const unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> kPfFirstShift, (unsigned)(kPfBins - 1));
     pf_red_add(hist + (d << 9));
   }
-  if (FIRST && !GEN) r.sum += (a[0] + a[1]) + (a[2] + a[3]);
+  r.sum += (a[0] + a[1]) + (a[2] + a[3]);
 }
 
-// Gather sweep, one chunk: the window's keys go to the row's slots, placed by a counter the row's two threads share
-// (the window holds at most 128 keys; a larger count is caught after the sweep).
-template <bool GEN, bool FULL>
-__device__ __forceinline__ void pf_gather_chunk(const uint32_t (&v)[32], uint32_t vm, const PfRow& r, uint32_t slots,
-                                                int* gcnt) {
+// Histogram sweep, generic chunk: candidates vm only, keys outside the row's window go to the sink bin. `first`: the
+// row's first sweep (fast-mode rows add up their scores).
+__device__ __forceinline__ void pf_hist_gen(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t hist, bool first) {
+  float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const bool sum = first && !r.gen;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const bool valid = FULL || ((vm >> j) & 1u);
-    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
-    if (valid && (unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) {
-      const int at = atomicAdd(gcnt, 1);
-      if (at < kPfGather) pf_st32(slots + ((uint32_t)at << 2), key);
-    }
+    const bool valid = (vm >> j) & 1u;
+    const int key = pf_key(v[j], r.gen);
+    a[j & 3] += (valid && sum) ? __uint_as_float(v[j]) : 0.0f;
+    unsigned d = min(((unsigned)r.top - (unsigned)min(key, r.top)) >> r.sh, (unsigned)(kPfBins - 1));
+    const bool in = valid && ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo);
+    d = in ? d : (unsigned)kPfBins;
+    pf_red_add(hist + (d << 9));
+  }
+  if (sum) r.sum += (a[0] + a[1]) + (a[2] + a[3]);
+}
+
+// Gather sweep: the window's keys go to the row's 128 slots, the lower-column thread filling them from the front and
+// the other from the back (the window holds at most 128 keys, so they never meet; the count is r.cnt). Stores are
+// predicated, not branched around.
+template <bool HOT>
+__device__ __forceinline__ void pf_gather_chunk(const uint32_t (&v)[32], uint32_t vm, PfRow& r, uint32_t base, int step) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int key = HOT ? (int)v[j] : pf_key(v[j], r.gen);
+    const bool in = (HOT || ((vm >> j) & 1u)) && ((unsigned)key - (unsigned)r.wlo <= (unsigned)r.whi - (unsigned)r.wlo) &&
+                    r.cnt < kPfGather;
+    pf_st32_if(base + (uint32_t)(r.cnt * step), key, in);
+    r.cnt += in ? 1 : 0;
   }
 }
 
-// Emit sweep, one chunk: bit j of `take` for a key above the threshold (every key at or above it unless TIE), bit j
-// of `eq` for a key equal to it (TIE only), both limited to the candidates.
-template <bool GEN, bool TIE>
-__device__ __forceinline__ void pf_emit_chunk(const uint32_t (&v)[32], uint32_t vm, const PfRow& r, uint32_t& take,
-                                              uint32_t& eq) {
+// Emit sweep: bit j of `take` for a key at or above the threshold (hot) or above it (generic, with ties in `eq`),
+// limited to the candidates.
+__device__ __forceinline__ void pf_emit_hot(const uint32_t (&v)[32], const PfRow& r, uint32_t& take) {
+  uint32_t t = 0;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) t |= ((int)v[j] >= r.thr ? 1u : 0u) << j;
+  take = t;
+}
+__device__ __forceinline__ void pf_emit_gen(const uint32_t (&v)[32], uint32_t vm, const PfRow& r, uint32_t& take,
+                                            uint32_t& eq) {
   uint32_t t = 0, e = 0;
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
-    const int key = GEN ? pf_canon(v[j]) : (int)v[j];
-    if (TIE) {
-      t |= (key > r.thr ? 1u : 0u) << j;
-      e |= (key == r.thr ? 1u : 0u) << j;
-    } else {
-      t |= (key >= r.thr ? 1u : 0u) << j;
-    }
+    const int key = pf_key(v[j], r.gen);
+    t |= ((r.tie ? key > r.thr : key >= r.thr) ? 1u : 0u) << j;
+    e |= (r.tie && key == r.thr ? 1u : 0u) << j;
   }
   take = t & vm;
   eq = e & vm;
@@ -378,23 +401,16 @@ __device__ void pf_sweep(int nt, int& g, bool first, PfRow& r, const PfCtx& c, u
         }
       }
       if (KIND == kPfNone || !act) continue;
+      const bool hot = full && !r.gen;
       if (KIND == kPfHist) {
-        if (first) {
-          if (r.gen) { if (full) pf_hist_chunk<true, true, true>(v, vm, r, c.hist); else pf_hist_chunk<true, false, true>(v, vm, r, c.hist); }
-          else { if (full) pf_hist_chunk<false, true, true>(v, vm, r, c.hist); else pf_hist_chunk<false, false, true>(v, vm, r, c.hist); }
-        } else {
-          if (r.gen) pf_hist_chunk<true, false, false>(v, vm, r, c.hist);
-          else pf_hist_chunk<false, false, false>(v, vm, r, c.hist);
-        }
+        if (hot && first) pf_hist_hot(v, r, c.hist);
+        else pf_hist_gen(v, vm, r, c.hist, first);
       } else if (KIND == kPfGatherSt) {
-        if (r.gen) { if (full) pf_gather_chunk<true, true>(v, vm, r, c.stage, c.gcnt); else pf_gather_chunk<true, false>(v, vm, r, c.stage, c.gcnt); }
-        else { if (full) pf_gather_chunk<false, true>(v, vm, r, c.stage, c.gcnt); else pf_gather_chunk<false, false>(v, vm, r, c.stage, c.gcnt); }
+        if (hot) pf_gather_chunk<true>(v, vm, r, c.gbase, c.gstep);
+        else pf_gather_chunk<false>(v, vm, r, c.gbase, c.gstep);
       } else if (KIND == kPfEmit) {
-        if (r.tie) {
-          if (r.gen) pf_emit_chunk<true, true>(v, vm, r, take[w], eq[w]); else pf_emit_chunk<false, true>(v, vm, r, take[w], eq[w]);
-        } else {
-          if (r.gen) pf_emit_chunk<true, false>(v, vm, r, take[w], eq[w]); else pf_emit_chunk<false, false>(v, vm, r, take[w], eq[w]);
-        }
+        if (hot && !r.tie) pf_emit_hot(v, r, take[w]);
+        else pf_emit_gen(v, vm, r, take[w], eq[w]);
       }
     }
     if (KIND == kPfEmit) pf_emit_tile(c, r, s_ex, g & 1, c0 + 64 * c.half, take, eq);
@@ -443,15 +459,15 @@ __device__ __forceinline__ void pf_refine(PfRow& r) {
 // After a gather sweep, one warp per row of 16 (rows 32 q + 16 half .. + 15): the exact need-th largest of the
 // gathered keys (an MSB-first bitwise select on the offsets whi - key), then the threshold, how many keys equal to it
 // the row takes and whether that is fewer than all of them; an overflowed row is marked.
-__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const int* s_gcnt,
+__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const int* s_gn,
                                            int* s_thr, int* s_eql, uint8_t* s_flag) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int rr = 0; rr < 16; ++rr) {
     const int ln = 16 * c.half + rr, row = 32 * c.q + ln;
     if (__shfl_sync(0xffffffffu, r.state, ln) != kPfGatherSt) continue;
-    const int n = s_gcnt[row];
-    if (n > kPfGather) { if (lane == 0) s_flag[row] = 2; continue; }
+    const int n0 = s_gn[row], n1 = s_gn[kPfRows + row];          // slots [0, n0) and [128 - n1, 128)
+    if (n0 + n1 > kPfGather) { if (lane == 0) s_flag[row] = 2; continue; }
     const int need = __shfl_sync(0xffffffffu, r.need, ln);
     const int whi = __shfl_sync(0xffffffffu, r.whi, ln);
     const int wlo = __shfl_sync(0xffffffffu, r.wlo, ln);
@@ -461,7 +477,7 @@ __device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint3
 #pragma unroll
     for (int qq = 0; qq < 4; ++qq) {
       const int i = lane + 32 * qq;
-      ok[qq] = i < n;
+      ok[qq] = i < n0 || i >= kPfGather - n1;
       o[qq] = ok[qq] ? (unsigned)whi - pf_ld32(slot + (uint32_t)i * 4) : 0u;
     }
     const unsigned span = (unsigned)whi - (unsigned)wlo;
@@ -502,7 +518,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   __shared__ volatile int s_abort;
   __shared__ uint32_t s_ex[2 * 2 * kPfRows];          // emit: [tile parity][half][row] counts
   __shared__ int s_thr[kPfRows], s_eql[kPfRows];
-  __shared__ int s_gcnt[kPfRows];
+  __shared__ int s_gn[2 * kPfRows];
   __shared__ uint8_t s_flag[kPfRows], s_bad[kPfRows];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -544,7 +560,7 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         const uint32_t dst = s_a + (uint32_t)(c.row >> 3) * 512u + (uint32_t)kc * 128u + (uint32_t)(c.row & 7) * 16u;
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst), "r"(w0), "r"(w1), "r"(w2), "r"(w3) : "memory");
       }
-      s_bad[c.row] = 0; s_flag[c.row] = 0; s_gcnt[c.row] = 0;
+      s_bad[c.row] = 0; s_flag[c.row] = 0;
     }
     for (uint32_t o = (uint32_t)tid * 16u; o < kPfWorkBytes; o += 2 * kPfRows * 16u)
       asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};\n" ::"r"(s_work + o), "r"(0) : "memory");
@@ -568,7 +584,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   c.tcol = tbase + ((uint32_t)(32 * c.q) << 16);
   c.hist = s_work + (uint32_t)c.row * 4u;
   c.stage = s_work + (uint32_t)c.row * (kPfGather * 4);
-  c.gcnt = &s_gcnt[c.row];
+  c.gbase = c.stage + (c.half ? (uint32_t)(kPfGather - 1) * 4u : 0u);
+  c.gstep = c.half ? -4 : 4;
   c.out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
   c.srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
   const uint64_t adesc0 = pf_sdesc(s_a, 128, 512, 0);
@@ -653,12 +670,12 @@ __global__ void __launch_bounds__(kPfThreads, 2)
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
         if (was)                                         // clear the row's bins (and its sink) for the next histogram
           for (int d = c.half * 65; d < min(kPfBins + 1, c.half * 65 + 65); ++d) pf_st32(c.hist + ((uint32_t)d << 9), 0);
-        if (c.half == 0) s_gcnt[c.row] = 0;
       } else if (kind == kPfGatherSt) {
         pf_sweep<kPfGatherSt>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
+        s_gn[c.half * kPfRows + c.row] = r.state == kPfGatherSt ? r.cnt : 0;
         if (tid == 0) s_anyovf = 0;
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
-        pf_resolve(r, c, s_work, s_gcnt, s_thr, s_eql, s_flag);
+        pf_resolve(r, c, s_work, s_gn, s_thr, s_eql, s_flag);
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
         if (r.state == kPfGatherSt) {
           const int f = s_flag[c.row];
