@@ -49,6 +49,7 @@ constexpr uint32_t kPfWorkBytes = kPfRows * (kPfBins + 1) * 4;       // histogra
 constexpr size_t kPfSmem = 1024 + kPfStages * kPfStageBytes + kPfABytes + kPfWorkBytes;
 
 static_assert(kPfStages % 2 == 0, "stage s is reused by the tile that reuses its TMEM buffer");
+static_assert(3 * 16 * 512 <= kPfStages * kPfStageBytes, "three sets of 16 digit counters per row fit in the copy stages");
 static_assert(kPfGather * kPfRows * 4 <= kPfWorkBytes && kPfStaged * kPfRows * 2 <= kPfWorkBytes, "work area");
 
 // Row states (one thread per row).
@@ -169,9 +170,10 @@ __device__ __forceinline__ int pf_ld16(uint32_t saddr) {
 struct PfCtx {
   uint32_t tcol;        // TMEM address of the warp's lane quarter, column 0
   uint32_t hist;        // the row's bin-0 word of the histogram (bins 512 bytes apart; bin kPfBins is a sink)
-  uint32_t stage;       // the row's 512-byte slot: 128 gathered keys, later 256 staged output positions (16-bit)
-  uint32_t gbase;       // this thread's first gather slot (half 0: slot 0, half 1: slot 127)
-  int gstep;            // +4 or -4 bytes per gathered key
+  uint32_t stage;       // the row's 512-byte slot of 256 staged output positions (16-bit)
+  uint32_t gbase;       // this thread's first gather slot (half 0: slot 0, half 1: slot 127; slot i of row r is word
+                        // i * 128 + r of the work area)
+  int gstep;            // +512 or -512 bytes per gathered key
   int* out;             // the row's output positions (used directly when k > kPfStaged)
   float* srow;          // the row's scores (optional)
   int half;             // 0: columns 0-63 of every tile, 1: columns 64-127
@@ -456,53 +458,73 @@ __device__ __forceinline__ void pf_refine(PfRow& r) {
   r.state = kPfHist; r.top = r.whi; r.sh = bits > 7 ? bits - 7 : 0;
 }
 
-// After a gather sweep, one warp per row of 16 (rows 32 q + 16 half .. + 15): the exact need-th largest of the
-// gathered keys (an MSB-first bitwise select on the offsets whi - key), then the threshold, how many keys equal to it
-// the row takes and whether that is fewer than all of them; an overflowed row is marked.
-__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, const int* s_gn,
-                                           int* s_thr, int* s_eql, uint8_t* s_flag) {
-  const int lane = threadIdx.x & 31;
+// After a gather sweep, both threads of each row: the exact need-th largest of the gathered keys, by a radix select on
+// the offsets o = whi - key, four bits per pass from the top: each thread adds its own keys that match the prefix so
+// far to the row's 16 digit counters, the pair meets at a named barrier, and both pick the digit holding the need-th
+// smallest offset. Counters live in the (idle) copy stages, three sets in turn so one barrier per pass suffices; the
+// gathered keys are read from their slots (slot i of row r at word i * 128 + r: the 32 rows of a warp hit 32 banks).
+// Then the threshold, how many keys equal to it the row takes and whether that is fewer than all of them; a row whose
+// threads gathered more than 128 keys is marked for a finer histogram.
+__device__ __forceinline__ void pf_resolve(const PfRow& r, const PfCtx& c, uint32_t s_work, uint32_t s_bins,
+                                           const int* s_gn, uint32_t* s_ex, int* s_thr, int* s_eql, uint8_t* s_flag) {
+  const bool act = r.state == kPfGatherSt;
+  const int n0 = s_gn[c.row], n1 = s_gn[kPfRows + c.row];          // slots [0, n0) and [128 - n1, 128)
+  const bool work = act && n0 + n1 <= kPfGather;
+  const unsigned whi = (unsigned)r.whi, span = whi - (unsigned)r.wlo;
+  const int bits = work ? 32 - __clz((int)(span | 1u)) : 0;
+  const int npass = ((int)__reduce_max_sync(0xffffffffu, (unsigned)bits) + 3) / 4;   // the same in both warps
+  const int mlo = c.half ? kPfGather - n1 : 0, mhi = c.half ? kPfGather : n0;
+  const uint32_t col = s_work + (uint32_t)c.row * 4u, bins = s_bins + (uint32_t)c.row * 4u;
+  unsigned pref = 0;
+  int rem = r.need;
 #pragma unroll 1
-  for (int rr = 0; rr < 16; ++rr) {
-    const int ln = 16 * c.half + rr, row = 32 * c.q + ln;
-    if (__shfl_sync(0xffffffffu, r.state, ln) != kPfGatherSt) continue;
-    const int n0 = s_gn[row], n1 = s_gn[kPfRows + row];          // slots [0, n0) and [128 - n1, 128)
-    if (n0 + n1 > kPfGather) { if (lane == 0) s_flag[row] = 2; continue; }
-    const int need = __shfl_sync(0xffffffffu, r.need, ln);
-    const int whi = __shfl_sync(0xffffffffu, r.whi, ln);
-    const int wlo = __shfl_sync(0xffffffffu, r.wlo, ln);
-    const uint32_t slot = s_work + (uint32_t)row * (kPfGather * 4);
-    unsigned o[4];
-    bool ok[4];
+  for (int pass = 0; pass < npass; ++pass) {
+    const int shift = 4 * (npass - 1 - pass);
+    const uint32_t cur = bins + (uint32_t)(pass % 3) * (16 * 512), nxt = bins + (uint32_t)((pass + 1) % 3) * (16 * 512);
 #pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-      const int i = lane + 32 * qq;
-      ok[qq] = i < n0 || i >= kPfGather - n1;
-      o[qq] = ok[qq] ? (unsigned)whi - pf_ld32(slot + (uint32_t)i * 4) : 0u;
+    for (int d = 0; d < 8; ++d) pf_st32(nxt + (uint32_t)(8 * c.half + d) * 512u, 0);
+    if (work) {
+#pragma unroll 4
+      for (int i = mlo; i < mhi; ++i) {
+        const unsigned o = whi - pf_ld32(col + (uint32_t)i * (kPfRows * 4));
+        const bool match = shift + 4 >= 32 || ((o ^ pref) >> (shift + 4)) == 0u;
+        if (match) pf_red_add(cur + (((o >> shift) & 15u) << 9));
+      }
     }
-    const unsigned span = (unsigned)whi - (unsigned)wlo;
-    unsigned pref = 0;
-    int rem = need;
+    asm volatile("bar.sync %0, 64;\n" ::"r"(2 + c.q) : "memory");
+    if (work) {
+      unsigned cum = 0;
+      int dig = 15;
 #pragma unroll 1
-    for (int bit = 31 - __clz((int)(span | 1u)); bit >= 0; --bit) {
-      int cnt = 0;
-#pragma unroll
-      for (int qq = 0; qq < 4; ++qq) cnt += (ok[qq] && ((o[qq] ^ pref) >> bit) == 0u) ? 1 : 0;
-      cnt = (int)__reduce_add_sync(0xffffffffu, (unsigned)cnt);
-      if (cnt < rem) { rem -= cnt; pref |= 1u << bit; }
+      for (int d = 0; d < 16; ++d) {
+        const unsigned n = pf_ld32(cur + (uint32_t)d * 512u);
+        if (cum + n >= (unsigned)rem) { dig = d; break; }
+        cum += n;
+      }
+      rem -= (int)cum;
+      pref |= (unsigned)dig << shift;
     }
-    int gt = 0, eq = 0;
-#pragma unroll
-    for (int qq = 0; qq < 4; ++qq) {
-      gt += (ok[qq] && o[qq] < pref) ? 1 : 0;
-      eq += (ok[qq] && o[qq] == pref) ? 1 : 0;
+  }
+  int gt = 0, eq = 0;
+  if (work) {
+#pragma unroll 4
+    for (int i = mlo; i < mhi; ++i) {
+      const unsigned o = whi - pf_ld32(col + (uint32_t)i * (kPfRows * 4));
+      gt += o < pref ? 1 : 0;
+      eq += o == pref ? 1 : 0;
     }
-    gt = (int)__reduce_add_sync(0xffffffffu, (unsigned)gt);
-    eq = (int)__reduce_add_sync(0xffffffffu, (unsigned)eq);
-    if (lane == 0) {
-      s_thr[row] = (int)((unsigned)whi - pref);
-      s_eql[row] = need - gt;
-      s_flag[row] = (need - gt) < eq ? 1 : 0;
+  }
+  s_ex[c.half * kPfRows + c.row] = (uint32_t)gt | ((uint32_t)eq << 16);
+  asm volatile("bar.sync %0, 64;\n" ::"r"(2 + c.q) : "memory");
+  if (c.half == 0 && act) {
+    if (!work) {
+      s_flag[c.row] = 2;
+    } else {
+      const uint32_t x0 = s_ex[c.row], x1 = s_ex[kPfRows + c.row];
+      const int gtt = (int)((x0 & 0xffffu) + (x1 & 0xffffu)), eqq = (int)((x0 >> 16) + (x1 >> 16));
+      s_thr[c.row] = (int)(whi - pref);
+      s_eql[c.row] = r.need - gtt;
+      s_flag[c.row] = (r.need - gtt) < eqq ? 1 : 0;
     }
   }
 }
@@ -584,8 +606,8 @@ __global__ void __launch_bounds__(kPfThreads, 2)
   c.tcol = tbase + ((uint32_t)(32 * c.q) << 16);
   c.hist = s_work + (uint32_t)c.row * 4u;
   c.stage = s_work + (uint32_t)c.row * (kPfGather * 4);
-  c.gbase = c.stage + (c.half ? (uint32_t)(kPfGather - 1) * 4u : 0u);
-  c.gstep = c.half ? -4 : 4;
+  c.gbase = s_work + (uint32_t)c.row * 4u + (c.half ? (uint32_t)(kPfGather - 1) * (kPfRows * 4) : 0u);
+  c.gstep = c.half ? -(kPfRows * 4) : kPfRows * 4;
   c.out = (row_thread && t < p.T) ? p.idx + ((size_t)head * p.T + t) * p.kcap : nullptr;
   c.srow = (p.scores && row_thread && t < p.T) ? p.scores + ((size_t)head * p.T + t) * p.C : nullptr;
   const uint64_t adesc0 = pf_sdesc(s_a, 128, 512, 0);
@@ -673,9 +695,11 @@ __global__ void __launch_bounds__(kPfThreads, 2)
       } else if (kind == kPfGatherSt) {
         pf_sweep<kPfGatherSt>(nt, g, first, r, c, s_tfull, s_tfree, s_ex, &s_abort, p.err);
         s_gn[c.half * kPfRows + c.row] = r.state == kPfGatherSt ? r.cnt : 0;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) pf_st32(s_stage + (uint32_t)c.row * 4u + (uint32_t)(8 * c.half + d) * 512u, 0);
         if (tid == 0) s_anyovf = 0;
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
-        pf_resolve(r, c, s_work, s_gn, s_thr, s_eql, s_flag);
+        pf_resolve(r, c, s_work, s_stage, s_gn, s_ex, s_thr, s_eql, s_flag);
         asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kPfRowWarps) : "memory");
         if (r.state == kPfGatherSt) {
           const int f = s_flag[c.row];
