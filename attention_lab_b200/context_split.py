@@ -127,6 +127,70 @@ class CudaContextOps:
         return _ops.lse_merge(all_parts, dtype)
 
 
+class PeerExchange:
+    """The protocol's two exchanges over peer memory instead of NCCL all-gathers.
+
+    Every rank allocates one region on its GPU (`ops.xchg_create`), the 64-byte CUDA IPC handles travel once over the
+    process group (`all_gather_object`), and every rank maps the others' regions (`ops.xchg_open`). Region layout:
+    two channels (0: keys, 1: partials), each with a flag word per rank (written by that rank, over NVLink) and an epoch
+    counter; then this rank's keys [B,G,k], its partials [B,G,h,d+2] and a gather area [world,B,G,k] for the threshold
+    kernel. Per layer a rank writes its keys into its region, signals channel 0, the threshold kernel waits for every
+    peer's flag and reads their keys; the same for the partials and the merge. Waits are bounded (`spin` polls of a
+    flag); a wait that gives up sets error bit 2 (`ops.device_status`). Collective: every rank constructs it with the
+    same shapes, and `close()` on every rank releases it."""
+
+    FLAGS = 256          # bytes per channel's flag array (64 ranks)
+
+    def __init__(self, B: int, G: int, k: int, h: int, d: int = 128, *, group=None, device=None, spin: int = 1 << 22):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if self.world > 64:
+            raise ValueError("at most 64 ranks")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.shape = (int(B), int(G), int(k), int(h), int(d))
+        self.spin = int(spin)
+        keys_b, parts_b = B * G * k * 8, B * G * h * (d + 2) * 4
+        al = lambda x: (x + 255) // 256 * 256
+        self.keys_off = 1024
+        self.parts_off = al(self.keys_off + keys_b)
+        self.gather_off = al(self.parts_off + parts_b)
+        nbytes = self.gather_off + self.world * keys_b
+        self.base, handle = _ops.xchg_create(nbytes, self.device)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle, group=group)
+        else:
+            handles[0] = handle
+        self.peers = [self.base if q == self.rank else _ops.xchg_open(handles[q], self.device) for q in range(self.world)]
+        dev = self.device
+        tab = lambda off: torch.tensor([b + off for b in self.peers], dtype=torch.int64, device=dev)
+        self.peer_flags = [tab(0), tab(self.FLAGS)]               # channel c's flag arrays on every rank
+        self.peer_keys, self.peer_parts = tab(self.keys_off), tab(self.parts_off)
+        self.flags = [self.base, self.base + self.FLAGS]         # this rank's flag arrays
+        self.counters = [self.base + 2 * self.FLAGS, self.base + 2 * self.FLAGS + 4]
+        self.keys = _ops.device_view(self.base + self.keys_off, (B, G, k), torch.int64, dev)
+        self.parts = _ops.device_view(self.base + self.parts_off, (B, G, h, d + 2), torch.float32, dev)
+        self.gather = _ops.device_view(self.base + self.gather_off, (self.world, B, G, k), torch.int64, dev)
+
+    def signal(self, channel: int) -> None:
+        _ops.xchg_signal(self.counters[channel], self.peer_flags[channel], self.world, self.rank)
+
+    def close(self) -> None:
+        """Collective: unmap the peers' regions, wait for every rank to have done the same, then free this rank's
+        region (synchronises the device first)."""
+        if self.base is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for q, ptr in enumerate(self.peers):
+            if q != self.rank:
+                _ops.xchg_close(ptr, self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        _ops.xchg_destroy(self.base, self.device)
+        self.base, self.peers = None, []
+
+
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
     if world == 1:
         return t.unsqueeze(0).contiguous()
@@ -137,12 +201,15 @@ def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
 
 
 def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan: ShardPlan, *,
-                              group=None, k_pre_new=None, scale=None, ops=None):
+                              group=None, k_pre_new=None, scale=None, ops=None, exchange: PeerExchange | None = None):
     """One layer's sparse decode step with the sequence split over the group's ranks (this rank holds the shard of
     `plan`: caches [B,G,shard_capacity,d] and zT [B,G,r,shard_capacity]). Every rank calls it with the same global
     step and gets the full output [B,G,h,1,d]; it equals decode.py:145-163 run on the unsplit caches. `k_pre_new`
     ([B,G,1,d], the newest key before RoPE) may be given on every rank: the rank whose shard holds position
-    legal_length - 1 writes its index column, the others ignore it."""
+    legal_length - 1 writes its index column, the others ignore it. With `exchange` (a PeerExchange of this group and
+    shape) the keys and partials move over peer memory instead of NCCL all-gathers."""
+    if exchange is not None:
+        return _peer_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan, exchange, k_pre_new, scale)
     ops = CudaContextOps if ops is None else ops
     world = plan.world
     if world > 1 and dist.get_world_size(group) != world:
@@ -162,3 +229,30 @@ def context_split_decode_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, 
     part = ops.attend_partial(q_main, k_cache, v_cache, rows, scale)
     all_parts = _all_gather(part, world, group)
     return ops.lse_merge(all_parts, q_main.dtype)
+
+
+def _peer_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan: ShardPlan, x: PeerExchange, k_pre_new,
+               scale):
+    """context_split_decode_step with the exchanges over peer memory (the same kernels around them)."""
+    B, G, h, _, d = q_main.shape
+    if x.world != plan.world or x.shape != (B, G, plan.k, h, d):
+        raise ValueError(f"exchange is for world {x.world} and shape {x.shape}, the step for world {plan.world} and "
+                         f"{(B, G, plan.k, h, d)}")
+    dev = q_main.device
+    kpn = k_pre_new if plan.write_col >= 0 else None
+    if plan.selected_count > 0:
+        rows, _ = _ops.context_local_topk(q_pre, zT, wq_t_scaled, wk, plan.fixed_rows(B, G, dev), plan.off_lo(B, G, dev),
+                                          plan.lo, plan.hi, plan.k_local, key_pos=plan.start, key_stride=plan.k,
+                                          k_pre_new=kpn, write_col=plan.write_col, keys_out=x.keys)
+    else:   # a shard past the legal range: nothing to score, nothing to attend
+        rows = torch.empty((B, G, 0), dtype=torch.int64, device=dev)
+        x.keys.zero_()
+    if plan.k > 0:   # the same on every rank
+        x.signal(0)
+        if plan.selected_count > 0:
+            rows = _ops.context_threshold_peer(x.peer_keys, x.gather, x.flags[0], x.counters[0], rows, plan.rank,
+                                               plan.k, plan.fixed_count, plan.k_local, spin=x.spin)
+    _ops.gathered_attend_partial(q_main, k_cache, v_cache, rows, scale=scale, part_out=x.parts)
+    x.signal(1)
+    return _ops.lse_merge_peer(x.peer_parts, x.flags[1], x.counters[1], plan.rank, (B, G, h, d), q_main.dtype,
+                               spin=x.spin)

@@ -34,6 +34,8 @@ int cuda_fail(cudaError_t e, const char* where) {
   return fail(AL_ECUDA, "%s: %s", where, cudaGetErrorString(e));
 }
 
+constexpr int kMaxRanks = 64;   // ranks of one exchange (the flag array of a channel holds one word each)
+
 struct DeviceInfo {
   int sms = 0;
   int max_smem_optin = 0;
@@ -723,6 +725,99 @@ int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void
   if (out_dtype == AL_BF16) lse_merge_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<__nv_bfloat16*>(out));
   else lse_merge_kernel<float><<<grid, 256, 0, st>>>(parts, world, (int)n, static_cast<float*>(out));
   return plain_launch_check("lse_merge_kernel");
+}
+
+int al_xchg_create(size_t bytes, void** region, void* handle_out) {
+  if (!region || !handle_out || bytes == 0) return fail(AL_EINVAL, "null pointer or empty region");
+  *region = nullptr;
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(exchange region)");
+  if ((e = cudaMemset(ptr, 0, bytes)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e, "cudaMemset(exchange region)"); }
+  cudaIpcMemHandle_t h;
+  if ((e = cudaIpcGetMemHandle(&h, ptr)) != cudaSuccess) { cudaFree(ptr); return cuda_fail(e, "cudaIpcGetMemHandle"); }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle_out, &h, sizeof(h));
+  *region = ptr;
+  return AL_OK;
+}
+
+int al_xchg_open(const void* handle, void** peer_region) {
+  if (!handle || !peer_region) return fail(AL_EINVAL, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void* ptr = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *peer_region = ptr;
+  return AL_OK;
+}
+
+int al_xchg_close(void* peer_region) {
+  if (!peer_region) return AL_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_region);
+  return e == cudaSuccess ? AL_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int al_xchg_destroy(void* region) {
+  if (!region) return AL_OK;
+  const cudaError_t e = cudaFree(region);
+  return e == cudaSuccess ? AL_OK : cuda_fail(e, "cudaFree(exchange region)");
+}
+
+int al_xchg_signal(unsigned* counter, unsigned* const* peer_flags, int world, int rank, void* stream) {
+  if (!counter || !peer_flags) return fail(AL_EINVAL, "null pointer argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
+  xchg_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counter, peer_flags, world, rank);
+  return plain_launch_check("xchg_signal_kernel");
+}
+
+int al_context_threshold_peer(const uint64_t* const* peer_keys, uint64_t* gather, const unsigned* flags,
+                              const unsigned* counter, int spin, int world, int rank, int B, int G, int key_stride,
+                              int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
+                              void* stream) {
+  if (!peer_keys || !gather || !flags || !counter || !rows_in || !rows_attend) return fail(AL_EINVAL, "null pointer argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
+  if (spin < 1) return fail(AL_EINVAL, "spin must be positive");
+  if (B <= 0 || G <= 0 || B * (long long)G > 0x7fffffffLL) return fail(AL_EINVAL, "B and G must be positive");
+  if (k < 1 || key_stride < 1 || k > (long long)world * key_stride)
+    return fail(AL_EINVAL, "k=%d must lie in [1, world*key_stride=%lld]", k, (long long)world * key_stride);
+  if (k_local < 0 || k_local > key_stride || fixed_count < 0)
+    return fail(AL_EINVAL, "k_local=%d must lie in [0, key_stride=%d]", k_local, key_stride);
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  CtxParams p = {};
+  p.P = world; p.B = B; p.G = G; p.kst = key_stride; p.k = k; p.rank = rank; p.F = fixed_count; p.k_local = k_local;
+  p.keys = reinterpret_cast<const unsigned long long*>(gather);
+  p.rows_in = reinterpret_cast<const long long*>(rows_in);
+  p.rows_attend = reinterpret_cast<long long*>(rows_attend);
+  p.peer_keys = reinterpret_cast<const unsigned long long* const*>(peer_keys);
+  p.wait = XchgWait{flags, counter, world, rank, spin, di->err};
+  // every rank launches it (its peers wait on nothing from it, but the grid must not depend on its own rows)
+  context_threshold_kernel<<<B * G, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return plain_launch_check("context_threshold_kernel");
+}
+
+int al_lse_merge_peer(const float* const* parts, const unsigned* flags, const unsigned* counter, int spin, int world,
+                      int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream) {
+  if (!parts || !flags || !counter || !out) return fail(AL_EINVAL, "null pointer argument");
+  if (!dtype_ok(out_dtype)) return fail(AL_EINVAL, "unknown dtype code");
+  if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
+  if (spin < 1) return fail(AL_EINVAL, "spin must be positive");
+  if (B <= 0 || G <= 0 || h <= 0) return fail(AL_EINVAL, "B, G and h must be positive");
+  const long long n = (long long)B * G * h;
+  if (n * kHeadDim > 0x7fffffffLL) return fail(AL_EUNSUPPORTED, "B*G*h too large");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  const XchgWait w{flags, counter, world, rank, spin, di->err};
+  const unsigned grid = (unsigned)((n * kHeadDim + 255) / 256);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (out_dtype == AL_BF16) lse_merge_peer_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(parts, w, (int)n, static_cast<__nv_bfloat16*>(out));
+  else lse_merge_peer_kernel<float><<<grid, 256, 0, st>>>(parts, w, (int)n, static_cast<float*>(out));
+  return plain_launch_check("lse_merge_peer_kernel");
 }
 
 int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,

@@ -9,11 +9,56 @@
 
 namespace al {
 
+// ------------------------------------------------------------------------------------------------ peer exchange
+// The ranks' exchange buffers (one cudaMalloc'd region per GPU, opened by the others through CUDA IPC) replace the two
+// NCCL all-gathers: a producer kernel writes into its own region, xchg_signal_kernel stores an epoch into every peer's
+// flag for this rank (system-scope release), and a consumer waits for every peer's flag to reach its own epoch
+// (system-scope acquire, bounded: a wait that gives up sets kErrWaitLimit and the launch's results are invalid) and
+// then reads the peers' data with plain loads over NVLink. The epoch is a device counter (one per channel) that the
+// signal kernel increments, so a captured CUDA graph replays with fresh epochs. A rank overwrites a region only after
+// a later step that needed every peer's data, so one slot per channel suffices.
+struct XchgWait {
+  const unsigned* flags;            // this rank's flags of the channel: flags[q] is written by rank q
+  const unsigned* counter;          // this rank's epoch counter of the channel (set by its signal kernel)
+  int P, rank, spin;                // spin: polls of one peer's flag before giving up
+  unsigned* err;
+};
+
+// Thread 0 of a CTA: wait until every peer's flag has reached this rank's epoch.
+__device__ __forceinline__ void xchg_wait(const XchgWait& w) {
+  const unsigned e = *reinterpret_cast<const volatile unsigned*>(w.counter);
+  for (int q = 0; q < w.P; ++q) {
+    if (q == w.rank) continue;
+    for (int it = 0;; ++it) {
+      unsigned f;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(f) : "l"(w.flags + q) : "memory");
+      if ((int)(f - e) >= 0) break;
+      if (it >= w.spin) { atomicOr(w.err, kErrWaitLimit); break; }
+      __nanosleep(128);
+    }
+  }
+}
+
+// One thread: advance this rank's epoch of the channel and publish it to every peer (after this stream's earlier
+// writes to the region, made visible system-wide first).
+__global__ void xchg_signal_kernel(unsigned* counter, unsigned* const* peer_flags, int P, int rank) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const unsigned e = *counter + 1u;
+  *counter = e;
+  __threadfence_system();
+  for (int q = 0; q < P; ++q)
+    if (q != rank) asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(peer_flags[q] + rank), "r"(e) : "memory");
+}
+
 struct CtxParams {
   int P, B, G, kst, k, rank, F, k_local;
   const unsigned long long* keys;   // [P, B, G, kst] all ranks' keys (zero padding below every real key)
   const long long* rows_in;         // [B, G, F + k_local] this rank's rows: F, then its candidates in key order
   long long* rows_attend;           // [B, G, F + k_local] the same rows, -1 where a candidate is not in the top-k
+  // peer exchange (peer_keys non-null): rank q's keys [B, G, kst] at peer_keys[q] (this rank's own among them); the
+  // CTA waits, then copies its segment of every rank's keys into `keys` (this rank's [P, B, G, kst] scratch)
+  const unsigned long long* const* peer_keys;
+  XchgWait wait;
 };
 
 // One CTA per (batch, group) segment: a radix select over the P * kst keys (six digits of 11/11/11/11/10/10 bits,
@@ -26,6 +71,17 @@ __global__ void __launch_bounds__(kThreads) context_threshold_kernel(const CtxPa
   const int seg = blockIdx.x, tid = threadIdx.x;
   if (tid == 0) { s_piv[0] = 0; s_piv[1] = 0; }
   const int BG = p.B * p.G, N = p.P * p.kst;
+  if (p.peer_keys) {
+    if (tid == 0) xchg_wait(p.wait);
+    __syncthreads();
+    unsigned long long* g = const_cast<unsigned long long*>(p.keys);
+    for (int q = 0; q < p.P; ++q) {
+      const unsigned long long* src = p.peer_keys[q] + (size_t)seg * p.kst;
+      unsigned long long* dst = g + ((size_t)q * BG + seg) * p.kst;
+      for (int j = tid; j < p.kst; j += kThreads) dst[j] = __ldcg(src + j);
+    }
+    __syncthreads();
+  }
   auto key_at = [&](int j) { return p.keys[((size_t)(j / p.kst) * BG + seg) * p.kst + (j % p.kst)]; };
   unsigned long long prefix = 0ull, pmask = 0ull;
   int need = p.k;
@@ -78,6 +134,35 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const float* __restrict_
       const float w = exp2f(pp[0] - M);
       L = fmaf(w, pp[1], L);
       A = fmaf(w, pp[2 + d], A);
+    }
+  }
+  out[idx] = fromf<T>(A / L);
+}
+
+// The same merge with rank q's partials [n, 130] at parts[q] (peer memory for q != rank), after a bounded wait for
+// every peer's flag by thread 0 of each block.
+template <typename T>
+__global__ void __launch_bounds__(256) lse_merge_peer_kernel(const float* const* __restrict__ parts, XchgWait w, int n,
+                                                              T* __restrict__ out) {
+  if (threadIdx.x == 0) xchg_wait(w);
+  __syncthreads();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * kHeadDim) return;
+  const int row = idx / kHeadDim, d = idx % kHeadDim;
+  float M = -INFINITY;
+  for (int q = 0; q < w.P; ++q) {
+    const float* pp = parts[q] + (size_t)row * (kHeadDim + 2);
+    const float l = __ldcg(pp + 1);
+    if (l > 0.f) M = fmaxf(M, __ldcg(pp));
+  }
+  float L = 0.f, A = 0.f;
+  for (int q = 0; q < w.P; ++q) {
+    const float* pp = parts[q] + (size_t)row * (kHeadDim + 2);
+    const float l = __ldcg(pp + 1);
+    if (l > 0.f) {
+      const float wq = exp2f(__ldcg(pp) - M);
+      L = fmaf(wq, l, L);
+      A = fmaf(wq, __ldcg(pp + 2 + d), A);
     }
   }
   out[idx] = fromf<T>(A / L);

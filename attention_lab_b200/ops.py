@@ -21,6 +21,8 @@ from __future__ import annotations
 
 import math
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -314,11 +316,12 @@ def append_kvz(k_cache, v_cache, zT, start: int, k_new, v_new, z_new=None, *, k_
 # context split across ranks (config C4): the device steps driven by attention_lab_b200.context_split
 # ---------------------------------------------------------------------------------------------------------------------
 def context_local_topk(q_pre, zT, wq_t_scaled, wk, fixed_rows, off_lo, lo: int, hi: int, k: int, *, key_pos: int,
-                       key_stride: int, k_pre_new=None, write_col: int = -1, cluster: int = 0):
+                       key_stride: int, k_pre_new=None, write_col: int = -1, cluster: int = 0, keys_out=None):
     """Local top-k of one shard's candidates [lo, hi): returns (rows [B,G,F+k] int64: F then the chosen candidates in
     ascending position order, as flat ids of the shard's cache; keys [B,G,key_stride] int64 holding the chosen
     candidates' 64-bit keys (score order key << 32 | 2^32-1 - (key_pos + column)), zero past k). Writes z of the
-    newest key into zT[..., write_col] when k_pre_new is given."""
+    newest key into zT[..., write_col] when k_pre_new is given. `keys_out` (int64 [B,G,key_stride], contiguous, e.g. a
+    view of a peer-exchange region) receives the keys instead of a new tensor."""
     dev = _cuda(q_pre, zT, wq_t_scaled, wk, fixed_rows, off_lo, k_pre_new)
     q_pre, psb, psg, psh = _q_strides(q_pre, "q_pre")
     B, G, h, _, d = q_pre.shape
@@ -346,7 +349,12 @@ def context_local_topk(q_pre, zT, wq_t_scaled, wk, fixed_rows, off_lo, lo: int, 
             k_pre_new = k_pre_new.contiguous()
         kn_sb, kn_sg = k_pre_new.stride(0), k_pre_new.stride(1)
     rows = torch.empty((B, G, F + k), dtype=torch.int64, device=dev)
-    keys = torch.empty((B, G, key_stride), dtype=torch.int64, device=dev)
+    if keys_out is None:
+        keys = torch.empty((B, G, key_stride), dtype=torch.int64, device=dev)
+    else:
+        if tuple(keys_out.shape) != (B, G, key_stride) or keys_out.dtype != torch.int64 or not keys_out.is_contiguous():
+            raise ValueError("keys_out must be a contiguous int64 [B,G,key_stride] tensor")
+        keys = keys_out
     lib = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(lib.al_context_local_topk(
@@ -376,9 +384,9 @@ def context_threshold(all_keys, rows, rank: int, k: int, fixed_count: int, k_loc
     return out
 
 
-def gathered_attend_partial(q_main, k_cache, v_cache, rows, *, scale=None, cluster: int = 0):
+def gathered_attend_partial(q_main, k_cache, v_cache, rows, *, scale=None, cluster: int = 0, part_out=None):
     """Unnormalised attention partial over rows [B,G,n] (flat ids of the cache, -1 = not read): returns float32
-    [B,G,h,130] = (m in the log2 domain, l, acc[128]) per head, for lse_merge."""
+    [B,G,h,130] = (m in the log2 domain, l, acc[128]) per head, for lse_merge (into `part_out` when given)."""
     dev = _cuda(q_main, k_cache, v_cache, rows)
     q_main, qsb, qsg, qsh = _q_strides(q_main, "q_main")
     B, G, h, _, d = q_main.shape
@@ -393,7 +401,12 @@ def gathered_attend_partial(q_main, k_cache, v_cache, rows, *, scale=None, clust
         raise ValueError("rows must be int64 with B*G*n elements")
     n = rows.numel() // (B * G)
     rows = rows.contiguous()
-    part = torch.empty((B, G, h, d + 2), dtype=torch.float32, device=dev)
+    if part_out is None:
+        part = torch.empty((B, G, h, d + 2), dtype=torch.float32, device=dev)
+    else:
+        if tuple(part_out.shape) != (B, G, h, d + 2) or part_out.dtype != torch.float32 or not part_out.is_contiguous():
+            raise ValueError("part_out must be a contiguous float32 [B,G,h,d+2] tensor")
+        part = part_out
     lib = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(lib.al_gathered_attend_partial(
@@ -415,6 +428,98 @@ def lse_merge(all_parts, dtype=torch.bfloat16):
     lib = _lib.load()
     with torch.cuda.device(dev):
         _lib.check(lib.al_lse_merge(all_parts.data_ptr(), world, B, G, h, d2 - 2, out.data_ptr(), code, _stream(dev)))
+    return out
+
+
+class _DeviceArray:
+    """A raw device pointer seen as an array (`__cuda_array_interface__`), for torch.as_tensor views."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(x) for x in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+def device_view(ptr: int, shape, dtype, device) -> torch.Tensor:
+    """A tensor over device memory the library allocated (no copy; the memory must outlive the tensor)."""
+    typestr = {torch.int64: "<i8", torch.float32: "<f4", torch.int32: "<i4"}[dtype]
+    with torch.cuda.device(device):
+        return torch.as_tensor(_DeviceArray(ptr, shape, typestr), device=device)
+
+
+def xchg_create(nbytes: int, device) -> tuple:
+    """A zero-filled exchange region of nbytes on `device` (al_xchg_create): (address, 64-byte CUDA IPC handle)."""
+    lib = _lib.load()
+    region, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+    with torch.cuda.device(device):
+        _lib.check(lib.al_xchg_create(int(nbytes), ctypes.byref(region), handle))
+    return int(region.value), bytes(handle)
+
+
+def xchg_open(handle: bytes, device) -> int:
+    """Map a peer's exchange region from its handle (al_xchg_open); returns its address in this process."""
+    if len(handle) != 64:
+        raise ValueError("an exchange handle is 64 bytes")
+    lib = _lib.load()
+    ptr = ctypes.c_void_p()
+    with torch.cuda.device(device):
+        _lib.check(lib.al_xchg_open(ctypes.create_string_buffer(handle, 64), ctypes.byref(ptr)))
+    return int(ptr.value)
+
+
+def xchg_close(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().al_xchg_close(ctypes.c_void_p(ptr)))
+
+
+def xchg_destroy(ptr: int, device) -> None:
+    with torch.cuda.device(device):
+        _lib.check(_lib.load().al_xchg_destroy(ctypes.c_void_p(ptr)))
+
+
+def xchg_signal(counter: int, peer_flags, world: int, rank: int) -> None:
+    """Advance this rank's epoch of a channel and publish it to every peer (al_xchg_signal); peer_flags is an int64
+    device tensor of the ranks' flag-array addresses."""
+    dev = peer_flags.device
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_xchg_signal(ctypes.c_void_p(counter), peer_flags.data_ptr(), int(world), int(rank),
+                                              _stream(dev)))
+
+
+def context_threshold_peer(peer_keys, gather, flags: int, counter: int, rows, rank: int, k: int, fixed_count: int,
+                           k_local: int, *, spin: int = 1 << 22):
+    """context_threshold reading every rank's keys [B,G,key_stride] from the addresses in peer_keys (int64 device
+    tensor, world entries) after a bounded wait on this rank's flags; gather [world,B,G,key_stride] is its scratch."""
+    dev = _cuda(peer_keys, gather, rows)
+    if gather.dim() != 4 or gather.dtype != torch.int64 or not gather.is_contiguous():
+        raise ValueError("gather must be a contiguous int64 [world,B,G,key_stride] tensor")
+    world, B, G, kst = gather.shape
+    if peer_keys.numel() != world or peer_keys.dtype != torch.int64:
+        raise ValueError("peer_keys must hold one int64 address per rank")
+    if tuple(rows.shape) != (B, G, fixed_count + k_local) or rows.dtype != torch.int64:
+        raise ValueError("rows must be int64 [B,G,fixed_count+k_local]")
+    rows = rows.contiguous()
+    out = torch.empty_like(rows)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_context_threshold_peer(
+            peer_keys.data_ptr(), gather.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin),
+            world, int(rank), B, G, kst, int(k), int(fixed_count), int(k_local), rows.data_ptr(), out.data_ptr(),
+            _stream(dev)))
+    return out
+
+
+def lse_merge_peer(peer_parts, flags: int, counter: int, rank: int, shape, dtype=torch.bfloat16, *, spin: int = 1 << 22):
+    """lse_merge reading every rank's partials [B,G,h,130] from the addresses in peer_parts after a bounded wait on
+    this rank's flags; shape = (B, G, h, d). Returns [B,G,h,1,d] of dtype."""
+    dev = _cuda(peer_parts)
+    B, G, h, d = (int(x) for x in shape)
+    code = _DTYPES.get(dtype)
+    if code is None:
+        raise ValueError(f"dtype must be float32 or bfloat16, got {dtype}")
+    out = torch.empty((B, G, h, 1, d), dtype=dtype, device=dev)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().al_lse_merge_peer(
+            peer_parts.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin), peer_parts.numel(),
+            int(rank), B, G, h, d, out.data_ptr(), code, _stream(dev)))
     return out
 
 

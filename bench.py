@@ -62,6 +62,8 @@ def parse():
     ap.add_argument("--context-split", action="store_true",
                     help="C4 measurement: one sequence split over the torchrun ranks (attention_lab_b200.context_split)")
     ap.add_argument("--no-graph", action="store_true", help="context split: launch every step from the host")
+    ap.add_argument("--exchange", choices=("peer", "nccl"), default="peer",
+                    help="context split: move keys and partials over peer memory (default) or NCCL all-gathers")
     ap.add_argument("--model", choices=["c2", "c3"], default=None,
                     help="end-to-end decode of a random-init Qwen3 through attention_lab_b200.runner: c2 (0.6B, 8192-token "
                          "prompt, 256 greedy steps) or c3 (8B shape, 32K context per request); sparse vs dense")
@@ -294,7 +296,8 @@ def config_of(args, desc, B, G, h, L, rho, layers):
 # ------------------------------------------------------------------------------------------------ GPU side
 def run_context_split(args):
     """One layer of C4 (B=1, L=131072, rho=1/32) with its positions split over the torchrun ranks: every timed step is
-    the whole protocol (local top-k, key all-gather, threshold, partial attend, partial all-gather, merge). Device
+    the whole protocol (local top-k, key exchange, threshold, partial attend, partial exchange, merge; the exchanges
+    over peer memory, or NCCL all-gathers with --exchange nccl). Device
     time per step with CUDA events, max over ranks; prints one JSON line (rank 0)."""
     import torch
     import torch.distributed as dist
@@ -320,8 +323,10 @@ def run_context_split(args):
     K, V, Z = rnd(B, G, cs_, D), rnd(B, G, cs_, D), rnd(B, G, R, cs_, scale=0.23)
     WQ, WK = rnd(G, h * D, R, scale=0.02 / math.sqrt(R)), rnd(G, R, D, scale=0.02)
     Q, QP, KPN = rnd(B, G, h, 1, D), rnd(B, G, h, 1, D), rnd(B, G, 1, D)
+    xchg = csplit.PeerExchange(B, G, plan.k, h, device=dev) if args.exchange == "peer" else None
+
     def step():    # every rank passes the newest key; the shard that owns position L - 1 writes its z column
-        return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=KPN)
+        return csplit.context_split_decode_step(Q, QP, K, V, Z, WQ, WK, plan, k_pre_new=KPN, exchange=xchg)
     side = torch.cuda.Stream(device=dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
@@ -358,11 +363,15 @@ def run_context_split(args):
                           "warmup": max(3, args.warmup), "higher_is_better": False, "scaling": "strong",
                           "dtype": "bf16", "data": "synthetic",
                           "config": {"workload": desc + f", split over {world} rank(s)", "k": lg["k"], "S": lg["S"],
-                                     "shard_capacity": cs_, "cuda_graph": graph is not None},
+                                     "shard_capacity": cs_, "cuda_graph": graph is not None,
+                                     "exchange": ("peer memory (NVLink loads, epoch flags)" if xchg is not None
+                                                  else "NCCL all-gathers") if world > 1 else "none (one rank)"},
                           "ledger_bytes": lg["d_s1_per_layer_request"],
                           "achieved_gbs_aggregate": round(lg["d_s1_per_layer_request"] / (ms * 1e-3) / 1e9, 1),
                           "peak_gbs_per_gpu": peak}))
     del graph, run                 # a graph holding NCCL work is released before the process group
+    if xchg is not None:
+        xchg.close()
     if world > 1:
         dist.destroy_process_group()
 

@@ -145,6 +145,36 @@ int al_gathered_attend_partial(const void* q_main, int64_t q_sb, int64_t q_sg, i
  *   the reference's partitioned attend, metal_attend.py:147-169. */
 int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
 
+/* ---- peer exchange for the context split (replaces the two all-gathers of the protocol above; no reference
+ * counterpart: the reference runs on one device). Every rank allocates one region with al_xchg_create, sends the
+ * 64-byte handle to the others (any host channel) and opens theirs with al_xchg_open; kernels then read peers'
+ * regions over NVLink. A region holds, at offsets the caller chooses: per channel a flag array (one uint32 per rank,
+ * written by that rank) and an epoch counter, and the data the channel publishes. */
+
+/* x1: cudaMalloc a zero-filled region of `bytes` on the current device; handle_out receives its 64-byte CUDA IPC
+ *   handle. */
+int al_xchg_create(size_t bytes, void** region, void* handle_out);
+/* x2: map a peer's region (its 64-byte handle) into this process; peer access is enabled on first use. */
+int al_xchg_open(const void* handle, void** peer_region);
+/* x3: unmap a peer's region (al_xchg_open) / free this rank's region (al_xchg_create). */
+int al_xchg_close(void* peer_region);
+int al_xchg_destroy(void* region);
+/* x4: advance this rank's epoch counter of a channel and store it into every peer's flag for this rank
+ *   (peer_flags: device array of world pointers to the ranks' flag arrays of the channel), after a system-scope
+ *   fence: everything this stream wrote before becomes visible to the peers first. */
+int al_xchg_signal(unsigned* counter, unsigned* const* peer_flags, int world, int rank, void* stream);
+/* x5: al_context_threshold reading every rank's keys [B,G,key_stride] from peer_keys (device array of world pointers,
+ *   this rank's own among them) once every peer's flag has reached this rank's epoch (bounded wait of `spin` polls per
+ *   peer; giving up sets error bit 2), gathered into `gather` [world,B,G,key_stride] (this rank's scratch). */
+int al_context_threshold_peer(const uint64_t* const* peer_keys, uint64_t* gather, const unsigned* flags,
+                              const unsigned* counter, int spin, int world, int rank, int B, int G, int key_stride,
+                              int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
+                              void* stream);
+/* x6: al_lse_merge reading every rank's partials [B,G,h,130] from parts (device array of world pointers), after the
+ *   same bounded wait. */
+int al_lse_merge_peer(const float* const* parts, const unsigned* flags, const unsigned* counter, int spin, int world,
+                      int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
+
 /* Batched prefill scorer (config C5). No single reference counterpart: the reference selects nothing during prefill
  * (qwen_wrap.py:287-289); this applies its decode-time selection (candidates of selection.py:71-79 at legal length
  * p + 1, top-k of decode.py:86-93, ties to the smaller position) to every query position p of a prefill chunk.
