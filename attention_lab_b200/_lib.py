@@ -71,13 +71,11 @@ SIGNATURES = {
     "al_xchg_open": [c_void_p, POINTER(c_void_p)],
     "al_xchg_close": [c_void_p],
     "al_xchg_destroy": [c_void_p],
-    "al_xchg_signal": [c_void_p, c_void_p, c_int, c_int, c_void_p],
-    "al_context_threshold_peer": [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
-                                  c_int, c_int, c_int, c_void_p, c_void_p, c_void_p],
+    "al_xchg_push": [c_void_p, ctypes.c_size_t, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p, c_void_p],
+    "al_context_threshold_peer": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+                                  c_int, c_int, c_void_p, c_void_p, c_void_p],
     "al_lse_merge_peer": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
                           c_int, c_void_p],
-    "al_prefill_score_topk": [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
-                              c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p],
 }
 
 _lib = None

@@ -131,13 +131,14 @@ class PeerExchange:
     """The protocol's two exchanges over peer memory instead of NCCL all-gathers.
 
     Every rank allocates one region on its GPU (`ops.xchg_create`), the 64-byte CUDA IPC handles travel once over the
-    process group (`all_gather_object`), and every rank maps the others' regions (`ops.xchg_open`). Region layout:
-    two channels (0: keys, 1: partials), each with a flag word per rank (written by that rank, over NVLink) and an epoch
-    counter; then this rank's keys [B,G,k], its partials [B,G,h,d+2] and a gather area [world,B,G,k] for the threshold
-    kernel. Per layer a rank writes its keys into its region, signals channel 0, the threshold kernel waits for every
-    peer's flag and reads their keys; the same for the partials and the merge. Waits are bounded (`spin` polls of a
-    flag); a wait that gives up sets error bit 2 (`ops.device_status`). Collective: every rank constructs it with the
-    same shapes, and `close()` on every rank releases it."""
+    process group (`all_gather_object`), and every rank maps the others' regions (`ops.xchg_open`). Region layout: a
+    header with, per channel (0: keys, 1: partials), a flag word per rank (written by that rank, over NVLink), an epoch
+    counter and a done counter; then this rank's keys [B,G,k] and partials [B,G,h,d+2], and per channel a gather area
+    with one slot per rank. Per layer a rank writes its keys, pushes them into its slot of every rank's gather area
+    (`ops.xchg_push`: remote stores, then the epoch flags), and the threshold kernel waits for every peer's flag and
+    reads its own gather area; the same for the partials and the merge. Waits are bounded (`spin` polls of a flag); a
+    wait that gives up sets error bit 2 (`_lib.device_status`). Collective: every rank constructs it with the same
+    shapes, and `close()` on every rank releases it."""
 
     FLAGS = 256          # bytes per channel's flag array (64 ranks)
 
@@ -154,8 +155,9 @@ class PeerExchange:
         al = lambda x: (x + 255) // 256 * 256
         self.keys_off = 1024
         self.parts_off = al(self.keys_off + keys_b)
-        self.gather_off = al(self.parts_off + parts_b)
-        nbytes = self.gather_off + self.world * keys_b
+        self.gkeys_off = al(self.parts_off + parts_b)
+        self.gparts_off = al(self.gkeys_off + self.world * keys_b)
+        nbytes = self.gparts_off + self.world * parts_b
         self.base, handle = _ops.xchg_create(nbytes, self.device)
         handles = [None] * self.world
         if self.world > 1:
@@ -166,15 +168,20 @@ class PeerExchange:
         dev = self.device
         tab = lambda off: torch.tensor([b + off for b in self.peers], dtype=torch.int64, device=dev)
         self.peer_flags = [tab(0), tab(self.FLAGS)]               # channel c's flag arrays on every rank
-        self.peer_keys, self.peer_parts = tab(self.keys_off), tab(self.parts_off)
+        self.peer_gather = [tab(self.gkeys_off), tab(self.gparts_off)]
         self.flags = [self.base, self.base + self.FLAGS]         # this rank's flag arrays
         self.counters = [self.base + 2 * self.FLAGS, self.base + 2 * self.FLAGS + 4]
+        self.done = [self.base + 2 * self.FLAGS + 8, self.base + 2 * self.FLAGS + 12]
         self.keys = _ops.device_view(self.base + self.keys_off, (B, G, k), torch.int64, dev)
         self.parts = _ops.device_view(self.base + self.parts_off, (B, G, h, d + 2), torch.float32, dev)
-        self.gather = _ops.device_view(self.base + self.gather_off, (self.world, B, G, k), torch.int64, dev)
+        self.gather_keys = _ops.device_view(self.base + self.gkeys_off, (self.world, B, G, k), torch.int64, dev)
+        self.gather_parts = _ops.device_view(self.base + self.gparts_off, (self.world, B, G, h, d + 2), torch.float32,
+                                             dev)
 
-    def signal(self, channel: int) -> None:
-        _ops.xchg_signal(self.counters[channel], self.peer_flags[channel], self.world, self.rank)
+    def push(self, channel: int) -> None:
+        src = self.keys if channel == 0 else self.parts
+        _ops.xchg_push(src, self.peer_gather[channel], self.rank, self.done[channel], self.counters[channel],
+                       self.peer_flags[channel])
 
     def close(self) -> None:
         """Collective: unmap the peers' regions, wait for every rank to have done the same, then free this rank's
@@ -248,11 +255,10 @@ def _peer_step(q_main, q_pre, k_cache, v_cache, zT, wq_t_scaled, wk, plan: Shard
         rows = torch.empty((B, G, 0), dtype=torch.int64, device=dev)
         x.keys.zero_()
     if plan.k > 0:   # the same on every rank
-        x.signal(0)
+        x.push(0)
         if plan.selected_count > 0:
-            rows = _ops.context_threshold_peer(x.peer_keys, x.gather, x.flags[0], x.counters[0], rows, plan.rank,
-                                               plan.k, plan.fixed_count, plan.k_local, spin=x.spin)
+            rows = _ops.context_threshold_peer(x.gather_keys, x.flags[0], x.counters[0], rows, plan.rank, plan.k,
+                                               plan.fixed_count, plan.k_local, spin=x.spin)
     _ops.gathered_attend_partial(q_main, k_cache, v_cache, rows, scale=scale, part_out=x.parts)
-    x.signal(1)
-    return _ops.lse_merge_peer(x.peer_parts, x.flags[1], x.counters[1], plan.rank, (B, G, h, d), q_main.dtype,
-                               spin=x.spin)
+    x.push(1)
+    return _ops.lse_merge_peer(x.gather_parts, x.flags[1], x.counters[1], plan.rank, q_main.dtype, spin=x.spin)

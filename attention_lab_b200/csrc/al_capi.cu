@@ -765,18 +765,28 @@ int al_xchg_destroy(void* region) {
   return e == cudaSuccess ? AL_OK : cuda_fail(e, "cudaFree(exchange region)");
 }
 
-int al_xchg_signal(unsigned* counter, unsigned* const* peer_flags, int world, int rank, void* stream) {
-  if (!counter || !peer_flags) return fail(AL_EINVAL, "null pointer argument");
+int al_xchg_push(const void* src, size_t bytes, void* const* dst, int world, int rank, unsigned* done,
+                 unsigned* counter, unsigned* const* peer_flags, void* stream) {
+  if (!src || !dst || !done || !counter || !peer_flags) return fail(AL_EINVAL, "null pointer argument");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
-  xchg_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counter, peer_flags, world, rank);
-  return plain_launch_check("xchg_signal_kernel");
+  if (bytes == 0 || bytes % 16 || (reinterpret_cast<uintptr_t>(src) & 15))
+    return fail(AL_EUNSUPPORTED, "the pushed data must be a positive multiple of 16 bytes starting on a 16-byte boundary");
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  XchgPush x{};
+  x.src = static_cast<const int4*>(src); x.n16 = (long long)(bytes / 16);
+  x.dst = reinterpret_cast<int4* const*>(dst); x.P = world; x.rank = rank;
+  x.done = done; x.counter = counter; x.peer_flags = peer_flags;
+  const long long blocks = std::min<long long>((x.n16 + 255) / 256, 4LL * di->sms);
+  xchg_push_kernel<<<(unsigned)blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(x);
+  return plain_launch_check("xchg_push_kernel");
 }
 
-int al_context_threshold_peer(const uint64_t* const* peer_keys, uint64_t* gather, const unsigned* flags,
-                              const unsigned* counter, int spin, int world, int rank, int B, int G, int key_stride,
-                              int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
-                              void* stream) {
-  if (!peer_keys || !gather || !flags || !counter || !rows_in || !rows_attend) return fail(AL_EINVAL, "null pointer argument");
+int al_context_threshold_peer(const uint64_t* gather, const unsigned* flags, const unsigned* counter, int spin,
+                              int world, int rank, int B, int G, int key_stride, int k, int fixed_count, int k_local,
+                              const int64_t* rows_in, int64_t* rows_attend, void* stream) {
+  if (!gather || !flags || !counter || !rows_in || !rows_attend) return fail(AL_EINVAL, "null pointer argument");
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
   if (spin < 1) return fail(AL_EINVAL, "spin must be positive");
   if (B <= 0 || G <= 0 || B * (long long)G > 0x7fffffffLL) return fail(AL_EINVAL, "B and G must be positive");
@@ -792,16 +802,14 @@ int al_context_threshold_peer(const uint64_t* const* peer_keys, uint64_t* gather
   p.keys = reinterpret_cast<const unsigned long long*>(gather);
   p.rows_in = reinterpret_cast<const long long*>(rows_in);
   p.rows_attend = reinterpret_cast<long long*>(rows_attend);
-  p.peer_keys = reinterpret_cast<const unsigned long long* const*>(peer_keys);
   p.wait = XchgWait{flags, counter, world, rank, spin, di->err};
-  // every rank launches it (its peers wait on nothing from it, but the grid must not depend on its own rows)
   context_threshold_kernel<<<B * G, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return plain_launch_check("context_threshold_kernel");
 }
 
-int al_lse_merge_peer(const float* const* parts, const unsigned* flags, const unsigned* counter, int spin, int world,
+int al_lse_merge_peer(const float* gather, const unsigned* flags, const unsigned* counter, int spin, int world,
                       int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream) {
-  if (!parts || !flags || !counter || !out) return fail(AL_EINVAL, "null pointer argument");
+  if (!gather || !flags || !counter || !out) return fail(AL_EINVAL, "null pointer argument");
   if (!dtype_ok(out_dtype)) return fail(AL_EINVAL, "unknown dtype code");
   if (d != kHeadDim) return fail(AL_EUNSUPPORTED, "head_dim must be %d, got %d", kHeadDim, d);
   if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
@@ -815,9 +823,9 @@ int al_lse_merge_peer(const float* const* parts, const unsigned* flags, const un
   const XchgWait w{flags, counter, world, rank, spin, di->err};
   const unsigned grid = (unsigned)((n * kHeadDim + 255) / 256);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (out_dtype == AL_BF16) lse_merge_peer_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(parts, w, (int)n, static_cast<__nv_bfloat16*>(out));
-  else lse_merge_peer_kernel<float><<<grid, 256, 0, st>>>(parts, w, (int)n, static_cast<float*>(out));
-  return plain_launch_check("lse_merge_peer_kernel");
+  if (out_dtype == AL_BF16) lse_merge_wait_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(gather, w, (int)n, static_cast<__nv_bfloat16*>(out));
+  else lse_merge_wait_kernel<float><<<grid, 256, 0, st>>>(gather, w, (int)n, static_cast<float*>(out));
+  return plain_launch_check("lse_merge_wait_kernel");
 }
 
 int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,

@@ -10,16 +10,18 @@
 namespace al {
 
 // ------------------------------------------------------------------------------------------------ peer exchange
-// The ranks' exchange buffers (one cudaMalloc'd region per GPU, opened by the others through CUDA IPC) replace the two
-// NCCL all-gathers: a producer kernel writes into its own region, xchg_signal_kernel stores an epoch into every peer's
-// flag for this rank (system-scope release), and a consumer waits for every peer's flag to reach its own epoch
-// (system-scope acquire, bounded: a wait that gives up sets kErrWaitLimit and the launch's results are invalid) and
-// then reads the peers' data with plain loads over NVLink. The epoch is a device counter (one per channel) that the
-// signal kernel increments, so a captured CUDA graph replays with fresh epochs. A rank overwrites a region only after
-// a later step that needed every peer's data, so one slot per channel suffices.
+// The ranks' exchange regions (one cudaMalloc'd region per GPU, mapped by the others through CUDA IPC) replace the two
+// NCCL all-gathers. A channel (keys, partials) has in every region a gather area with one slot per rank, a flag word
+// per rank and an epoch counter. xchg_push_kernel copies this rank's data into its slot of every rank's gather area
+// (stores over NVLink, which do not stall the copying threads), and the last CTA to finish advances this rank's epoch
+// and stores it into every peer's flag for this rank (system-scope fences before the release stores: the data is
+// visible first). A consumer waits for every peer's flag to reach its own epoch (system-scope acquire, bounded: a wait
+// that gives up sets kErrWaitLimit and the launch's results are invalid) and reads only its own gather area. The
+// epoch lives on the device, so a captured CUDA graph replays with fresh epochs. A rank pushes into a slot again only
+// after a later step that needed every peer's data, so one slot per rank and channel suffices.
 struct XchgWait {
   const unsigned* flags;            // this rank's flags of the channel: flags[q] is written by rank q
-  const unsigned* counter;          // this rank's epoch counter of the channel (set by its signal kernel)
+  const unsigned* counter;          // this rank's epoch counter of the channel (set by its push)
   int P, rank, spin;                // spin: polls of one peer's flag before giving up
   unsigned* err;
 };
@@ -39,15 +41,34 @@ __device__ __forceinline__ void xchg_wait(const XchgWait& w) {
   }
 }
 
-// One thread: advance this rank's epoch of the channel and publish it to every peer (after this stream's earlier
-// writes to the region, made visible system-wide first).
-__global__ void xchg_signal_kernel(unsigned* counter, unsigned* const* peer_flags, int P, int rank) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const unsigned e = *counter + 1u;
-  *counter = e;
+struct XchgPush {
+  const int4* src;                  // this rank's data (n16 16-byte words)
+  long long n16;
+  int4* const* dst;                 // [P] the ranks' gather areas of the channel; this rank's slot at + rank * n16
+  int P, rank;
+  unsigned* done;                   // CTAs finished with the copy (this rank's region; reset by the last one)
+  unsigned* counter;                // this rank's epoch counter of the channel
+  unsigned* const* peer_flags;      // [P] the ranks' flag arrays of the channel
+};
+
+__global__ void __launch_bounds__(256) xchg_push_kernel(const XchgPush x) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < x.n16; i += stride) {
+    const int4 v = x.src[i];
+    for (int q = 0; q < x.P; ++q) x.dst[q][(long long)x.rank * x.n16 + i] = v;
+  }
   __threadfence_system();
-  for (int q = 0; q < P; ++q)
-    if (q != rank) asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(peer_flags[q] + rank), "r"(e) : "memory");
+  __syncthreads();
+  __shared__ bool s_last;
+  if (threadIdx.x == 0) s_last = atomicAdd(x.done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last || threadIdx.x != 0) return;
+  *x.done = 0u;
+  __threadfence_system();
+  const unsigned e = *x.counter + 1u;
+  *x.counter = e;
+  for (int q = 0; q < x.P; ++q)
+    if (q != x.rank) asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(x.peer_flags[q] + x.rank), "r"(e) : "memory");
 }
 
 struct CtxParams {
@@ -55,9 +76,8 @@ struct CtxParams {
   const unsigned long long* keys;   // [P, B, G, kst] all ranks' keys (zero padding below every real key)
   const long long* rows_in;         // [B, G, F + k_local] this rank's rows: F, then its candidates in key order
   long long* rows_attend;           // [B, G, F + k_local] the same rows, -1 where a candidate is not in the top-k
-  // peer exchange (peer_keys non-null): rank q's keys [B, G, kst] at peer_keys[q] (this rank's own among them); the
-  // CTA waits, then copies its segment of every rank's keys into `keys` (this rank's [P, B, G, kst] scratch)
-  const unsigned long long* const* peer_keys;
+  // peer exchange (wait.flags non-null): `keys` is this rank's gather area, filled by the ranks' pushes; the CTA waits
+  // for every peer's flag first
   XchgWait wait;
 };
 
@@ -71,15 +91,8 @@ __global__ void __launch_bounds__(kThreads) context_threshold_kernel(const CtxPa
   const int seg = blockIdx.x, tid = threadIdx.x;
   if (tid == 0) { s_piv[0] = 0; s_piv[1] = 0; }
   const int BG = p.B * p.G, N = p.P * p.kst;
-  if (p.peer_keys) {
+  if (p.wait.flags) {
     if (tid == 0) xchg_wait(p.wait);
-    __syncthreads();
-    unsigned long long* g = const_cast<unsigned long long*>(p.keys);
-    for (int q = 0; q < p.P; ++q) {
-      const unsigned long long* src = p.peer_keys[q] + (size_t)seg * p.kst;
-      unsigned long long* dst = g + ((size_t)q * BG + seg) * p.kst;
-      for (int j = tid; j < p.kst; j += kThreads) dst[j] = __ldcg(src + j);
-    }
     __syncthreads();
   }
   auto key_at = [&](int j) { return p.keys[((size_t)(j / p.kst) * BG + seg) * p.kst + (j % p.kst)]; };
@@ -139,10 +152,10 @@ __global__ void __launch_bounds__(256) lse_merge_kernel(const float* __restrict_
   out[idx] = fromf<T>(A / L);
 }
 
-// The same merge with rank q's partials [n, 130] at parts[q] (peer memory for q != rank), after a bounded wait for
-// every peer's flag by thread 0 of each block.
+// The same merge over this rank's gather area of partials, filled by the ranks' pushes, after a bounded wait for every
+// peer's flag by thread 0 of each block.
 template <typename T>
-__global__ void __launch_bounds__(256) lse_merge_peer_kernel(const float* const* __restrict__ parts, XchgWait w, int n,
+__global__ void __launch_bounds__(256) lse_merge_wait_kernel(const float* __restrict__ parts, XchgWait w, int n,
                                                               T* __restrict__ out) {
   if (threadIdx.x == 0) xchg_wait(w);
   __syncthreads();
@@ -151,18 +164,16 @@ __global__ void __launch_bounds__(256) lse_merge_peer_kernel(const float* const*
   const int row = idx / kHeadDim, d = idx % kHeadDim;
   float M = -INFINITY;
   for (int q = 0; q < w.P; ++q) {
-    const float* pp = parts[q] + (size_t)row * (kHeadDim + 2);
-    const float l = __ldcg(pp + 1);
-    if (l > 0.f) M = fmaxf(M, __ldcg(pp));
+    const float* pp = parts + ((size_t)q * n + row) * (kHeadDim + 2);
+    if (pp[1] > 0.f) M = fmaxf(M, pp[0]);
   }
   float L = 0.f, A = 0.f;
   for (int q = 0; q < w.P; ++q) {
-    const float* pp = parts[q] + (size_t)row * (kHeadDim + 2);
-    const float l = __ldcg(pp + 1);
-    if (l > 0.f) {
-      const float wq = exp2f(__ldcg(pp) - M);
-      L = fmaf(wq, l, L);
-      A = fmaf(wq, __ldcg(pp + 2 + d), A);
+    const float* pp = parts + ((size_t)q * n + row) * (kHeadDim + 2);
+    if (pp[1] > 0.f) {
+      const float wq = exp2f(pp[0] - M);
+      L = fmaf(wq, pp[1], L);
+      A = fmaf(wq, pp[2 + d], A);
     }
   }
   out[idx] = fromf<T>(A / L);

@@ -476,50 +476,53 @@ def xchg_destroy(ptr: int, device) -> None:
         _lib.check(_lib.load().al_xchg_destroy(ctypes.c_void_p(ptr)))
 
 
-def xchg_signal(counter: int, peer_flags, world: int, rank: int) -> None:
-    """Advance this rank's epoch of a channel and publish it to every peer (al_xchg_signal); peer_flags is an int64
-    device tensor of the ranks' flag-array addresses."""
-    dev = peer_flags.device
+def xchg_push(src: torch.Tensor, dst, rank: int, done: int, counter: int, peer_flags) -> None:
+    """Copy src (contiguous, a multiple of 16 bytes) into slot `rank` of every rank's gather area (dst: int64 device
+    tensor of the ranks' gather-area addresses), then publish this rank's next epoch of the channel to every peer
+    (al_xchg_push)."""
+    dev = _cuda(src, dst, peer_flags)
+    if not src.is_contiguous():
+        raise ValueError("the pushed tensor must be contiguous")
     with torch.cuda.device(dev):
-        _lib.check(_lib.load().al_xchg_signal(ctypes.c_void_p(counter), peer_flags.data_ptr(), int(world), int(rank),
-                                              _stream(dev)))
+        _lib.check(_lib.load().al_xchg_push(src.data_ptr(), src.numel() * src.element_size(), dst.data_ptr(),
+                                            dst.numel(), int(rank), ctypes.c_void_p(done), ctypes.c_void_p(counter),
+                                            peer_flags.data_ptr(), _stream(dev)))
 
 
-def context_threshold_peer(peer_keys, gather, flags: int, counter: int, rows, rank: int, k: int, fixed_count: int,
-                           k_local: int, *, spin: int = 1 << 22):
-    """context_threshold reading every rank's keys [B,G,key_stride] from the addresses in peer_keys (int64 device
-    tensor, world entries) after a bounded wait on this rank's flags; gather [world,B,G,key_stride] is its scratch."""
-    dev = _cuda(peer_keys, gather, rows)
+def context_threshold_peer(gather, flags: int, counter: int, rows, rank: int, k: int, fixed_count: int, k_local: int,
+                           *, spin: int = 1 << 22):
+    """context_threshold over this rank's gather area of keys [world,B,G,key_stride] (filled by the ranks' xchg_push)
+    once every peer's flag has reached this rank's epoch (bounded wait)."""
+    dev = _cuda(gather, rows)
     if gather.dim() != 4 or gather.dtype != torch.int64 or not gather.is_contiguous():
         raise ValueError("gather must be a contiguous int64 [world,B,G,key_stride] tensor")
     world, B, G, kst = gather.shape
-    if peer_keys.numel() != world or peer_keys.dtype != torch.int64:
-        raise ValueError("peer_keys must hold one int64 address per rank")
     if tuple(rows.shape) != (B, G, fixed_count + k_local) or rows.dtype != torch.int64:
         raise ValueError("rows must be int64 [B,G,fixed_count+k_local]")
     rows = rows.contiguous()
     out = torch.empty_like(rows)
     with torch.cuda.device(dev):
         _lib.check(_lib.load().al_context_threshold_peer(
-            peer_keys.data_ptr(), gather.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin),
-            world, int(rank), B, G, kst, int(k), int(fixed_count), int(k_local), rows.data_ptr(), out.data_ptr(),
-            _stream(dev)))
+            gather.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin), world, int(rank), B, G,
+            kst, int(k), int(fixed_count), int(k_local), rows.data_ptr(), out.data_ptr(), _stream(dev)))
     return out
 
 
-def lse_merge_peer(peer_parts, flags: int, counter: int, rank: int, shape, dtype=torch.bfloat16, *, spin: int = 1 << 22):
-    """lse_merge reading every rank's partials [B,G,h,130] from the addresses in peer_parts after a bounded wait on
-    this rank's flags; shape = (B, G, h, d). Returns [B,G,h,1,d] of dtype."""
-    dev = _cuda(peer_parts)
-    B, G, h, d = (int(x) for x in shape)
+def lse_merge_peer(gather, flags: int, counter: int, rank: int, dtype=torch.bfloat16, *, spin: int = 1 << 22):
+    """lse_merge over this rank's gather area of partials [world,B,G,h,d+2] once every peer's flag has reached this
+    rank's epoch (bounded wait). Returns [B,G,h,1,d] of dtype."""
+    dev = _cuda(gather)
+    if gather.dim() != 5 or gather.dtype != torch.float32 or not gather.is_contiguous():
+        raise ValueError("gather must be a contiguous float32 [world,B,G,h,d+2] tensor")
+    world, B, G, h, d2 = gather.shape
     code = _DTYPES.get(dtype)
     if code is None:
         raise ValueError(f"dtype must be float32 or bfloat16, got {dtype}")
-    out = torch.empty((B, G, h, 1, d), dtype=dtype, device=dev)
+    out = torch.empty((B, G, h, 1, d2 - 2), dtype=dtype, device=dev)
     with torch.cuda.device(dev):
         _lib.check(_lib.load().al_lse_merge_peer(
-            peer_parts.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin), peer_parts.numel(),
-            int(rank), B, G, h, d, out.data_ptr(), code, _stream(dev)))
+            gather.data_ptr(), ctypes.c_void_p(flags), ctypes.c_void_p(counter), int(spin), world, int(rank), B, G, h,
+            d2 - 2, out.data_ptr(), code, _stream(dev)))
     return out
 
 

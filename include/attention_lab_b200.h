@@ -147,9 +147,9 @@ int al_lse_merge(const float* parts, int world, int B, int G, int h, int d, void
 
 /* ---- peer exchange for the context split (replaces the two all-gathers of the protocol above; no reference
  * counterpart: the reference runs on one device). Every rank allocates one region with al_xchg_create, sends the
- * 64-byte handle to the others (any host channel) and opens theirs with al_xchg_open; kernels then read peers'
- * regions over NVLink. A region holds, at offsets the caller chooses: per channel a flag array (one uint32 per rank,
- * written by that rank) and an epoch counter, and the data the channel publishes. */
+ * 64-byte handle to the others (any host channel) and opens theirs with al_xchg_open. A region holds, at offsets the
+ * caller chooses, per channel (keys, partials): a gather area with one slot per rank, a flag word per rank (written by
+ * that rank over NVLink), an epoch counter and a done counter. */
 
 /* x1: cudaMalloc a zero-filled region of `bytes` on the current device; handle_out receives its 64-byte CUDA IPC
  *   handle. */
@@ -159,35 +159,21 @@ int al_xchg_open(const void* handle, void** peer_region);
 /* x3: unmap a peer's region (al_xchg_open) / free this rank's region (al_xchg_create). */
 int al_xchg_close(void* peer_region);
 int al_xchg_destroy(void* region);
-/* x4: advance this rank's epoch counter of a channel and store it into every peer's flag for this rank
- *   (peer_flags: device array of world pointers to the ranks' flag arrays of the channel), after a system-scope
- *   fence: everything this stream wrote before becomes visible to the peers first. */
-int al_xchg_signal(unsigned* counter, unsigned* const* peer_flags, int world, int rank, void* stream);
-/* x5: al_context_threshold reading every rank's keys [B,G,key_stride] from peer_keys (device array of world pointers,
- *   this rank's own among them) once every peer's flag has reached this rank's epoch (bounded wait of `spin` polls per
- *   peer; giving up sets error bit 2), gathered into `gather` [world,B,G,key_stride] (this rank's scratch). */
-int al_context_threshold_peer(const uint64_t* const* peer_keys, uint64_t* gather, const unsigned* flags,
-                              const unsigned* counter, int spin, int world, int rank, int B, int G, int key_stride,
-                              int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
-                              void* stream);
-/* x6: al_lse_merge reading every rank's partials [B,G,h,130] from parts (device array of world pointers), after the
- *   same bounded wait. */
-int al_lse_merge_peer(const float* const* parts, const unsigned* flags, const unsigned* counter, int spin, int world,
+/* x4: push `bytes` (a multiple of 16) from src into slot `rank` of every rank's gather area of a channel
+ *   (dst: device array of the world ranks' gather-area addresses; the slot is at dst[q] + rank * bytes), then, once
+ *   every copy is visible
+ *   system-wide, advance this rank's epoch counter of the channel and store it into every peer's flag for this rank
+ *   (peer_flags: device array of world addresses of the ranks' flag arrays; done: a zeroed word of this rank's). */
+int al_xchg_push(const void* src, size_t bytes, void* const* dst, int world, int rank, unsigned* done,
+                 unsigned* counter, unsigned* const* peer_flags, void* stream);
+/* x5: al_context_threshold over this rank's gather area of keys [world,B,G,key_stride] once every peer's flag of the
+ *   channel has reached this rank's epoch (bounded wait of `spin` polls per peer; giving up sets error bit 2). */
+int al_context_threshold_peer(const uint64_t* gather, const unsigned* flags, const unsigned* counter, int spin,
+                              int world, int rank, int B, int G, int key_stride, int k, int fixed_count, int k_local,
+                              const int64_t* rows_in, int64_t* rows_attend, void* stream);
+/* x6: al_lse_merge over this rank's gather area of partials [world,B,G,h,130], after the same bounded wait. */
+int al_lse_merge_peer(const float* gather, const unsigned* flags, const unsigned* counter, int spin, int world,
                       int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
-
-/* Batched prefill scorer (config C5). No single reference counterpart: the reference selects nothing during prefill
- * (qwen_wrap.py:287-289); this applies its decode-time selection (candidates of selection.py:71-79 at legal length
- * p + 1, top-k of decode.py:86-93, ties to the smaller position) to every query position p of a prefill chunk.
- *
- * u [H, T, r] bf16 (element strides u_sh, u_st; r = 32), zT [H, r, C] bf16 (strides z_sh, z_ld; C, z_sh, z_ld multiples
- * of 8, 16-byte aligned). Query row t sits at position q_pos0 + t (q_pos0 + T <= min(C, 65536)). For every (head,
- * row): idx_out[(h*T + t)*kcap + j] = the chosen candidate positions in ascending order (min(k, M) of them, M the
- * row's candidate count), -1 in the remaining slots up to kcap (k <= kcap). scores_out, when not NULL, is [H, T, C]
- * fp32 and receives the scores of every candidate column (other entries untouched). Scores are bf16 products with
- * fp32 accumulation on the tensor cores. */
-int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,
-                          int H, int T, int C, int r, int q_pos0, int k, int kcap, int* idx_out, float* scores_out,
-                          void* stream);
 
 #ifdef __cplusplus
 }

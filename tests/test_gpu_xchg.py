@@ -1,6 +1,6 @@
 """GPU tests of the context split's peer exchange (al_xchg_*, al_context_threshold_peer, al_lse_merge_peer): the two
-all-gathers of the C4 protocol replaced by writes into each rank's own region, epoch flags stored into the peers'
-regions, and reads of the peers' regions over NVLink.
+all-gathers of the C4 protocol replaced by pushes into every rank's gather area over NVLink, epoch flags stored into
+the peers' regions, and consumers that wait for the flags and read their own gather area.
 
 - one rank: the step through a PeerExchange equals the step without one, bit for bit;
 - a wait whose flag nothing sets gives up after its poll limit, sets error bit 2 and leaves the context usable;
@@ -51,23 +51,25 @@ def test_peer_exchange_on_one_rank_equals_the_plain_step():
 
 
 def test_a_wait_on_a_flag_nothing_sets_gives_up_with_an_error_bit():
-    """Two ranks' tables on one GPU, both entries this process's own region: this rank signals (its counter reaches 1)
+    """Two ranks' tables on one GPU, both entries this process's own region: this rank pushes (its counter reaches 1)
     but 'rank 1' never does, so the consumers' waits run out after `spin` polls."""
     from attention_lab_b200 import _lib, ops
     B, G, k, h, d = 1, 2, 64, 4, 128
     base, _ = ops.xchg_create(1 << 20, DEV)
     try:
         _lib.device_status()                                   # clear earlier bits
-        flags, counter = base, base + 512
+        flags, counter, done = base, base + 512, base + 520
         peer_flags = torch.tensor([base, base], dtype=torch.int64, device=DEV)
-        ops.xchg_signal(counter, peer_flags, 2, 0)
-        keys_at = torch.tensor([base + 4096, base + 4096], dtype=torch.int64, device=DEV)
-        gather = torch.zeros(2, B, G, k, dtype=torch.int64, device=DEV)
+        gkeys = ops.device_view(base + 4096, (2, B, G, k), torch.int64, DEV)
+        dst = torch.tensor([base + 4096, base + 4096], dtype=torch.int64, device=DEV)
+        ops.xchg_push(torch.ones(B, G, k, dtype=torch.int64, device=DEV), dst, 0, done, counter, peer_flags)
+        torch.cuda.synchronize()
+        assert int(gkeys[0].sum()) == B * G * k and int(gkeys[1].sum()) == 0, "the push fills slot 0 only"
         rows = torch.arange(B * G * k, dtype=torch.int64, device=DEV).view(B, G, k)
-        ops.context_threshold_peer(keys_at, gather, flags, counter, rows, 0, k, 0, k, spin=200)
+        ops.context_threshold_peer(gkeys, flags, counter, rows, 0, k, 0, k, spin=200)
         assert _lib.device_status() & 2, "the threshold wait must give up and flag it"
-        parts_at = torch.tensor([base + 65536, base + 65536], dtype=torch.int64, device=DEV)
-        ops.lse_merge_peer(parts_at, flags, counter, 0, (B, G, h, d), torch.float32, spin=200)
+        gparts = ops.device_view(base + 65536, (2, B, G, h, d + 2), torch.float32, DEV)
+        ops.lse_merge_peer(gparts, flags, counter, 0, torch.float32, spin=200)
         assert _lib.device_status() & 2, "the merge wait must give up and flag it"
         x = torch.ones(1000, device=DEV)                       # the context is still usable
         assert float((x * 2).sum()) == 2000.0
