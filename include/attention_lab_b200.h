@@ -175,6 +175,20 @@ int al_context_threshold_peer(const uint64_t* gather, const unsigned* flags, con
 int al_lse_merge_peer(const float* gather, const unsigned* flags, const unsigned* counter, int spin, int world,
                       int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
 
+/* Batched prefill scorer (config C5). No single reference counterpart: the reference selects nothing during prefill
+ * (qwen_wrap.py:287-289); this applies its decode-time selection (candidates of selection.py:71-79 at legal length
+ * p + 1, top-k of decode.py:86-93, ties to the smaller position) to every query position p of a prefill chunk.
+ *
+ * u [H, T, r] bf16 (element strides u_sh, u_st; r = 32), zT [H, r, C] bf16 (strides z_sh, z_ld; C, z_sh, z_ld multiples
+ * of 8, 16-byte aligned). Query row t sits at position q_pos0 + t (q_pos0 + T <= min(C, 65536)). For every (head,
+ * row): idx_out[(h*T + t)*kcap + j] = the chosen candidate positions in ascending order (min(k, M) of them, M the
+ * row's candidate count), -1 in the remaining slots up to kcap (k <= kcap). scores_out, when not NULL, is [H, T, C]
+ * fp32 and receives the scores of every candidate column (other entries untouched). Scores are bf16 products with
+ * fp32 accumulation on the tensor cores. */
+int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,
+                          int H, int T, int C, int r, int q_pos0, int k, int kcap, int* idx_out, float* scores_out,
+                          void* stream);
+
 #ifdef __cplusplus
 }
 #endif
