@@ -76,6 +76,8 @@ SIGNATURES = {
                                   c_int, c_int, c_void_p, c_void_p, c_void_p],
     "al_lse_merge_peer": [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
                           c_int, c_void_p],
+    "al_context_threshold_noalloc": [c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                     c_void_p, c_void_p],
     "al_prefill_score_topk": [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
                               c_int, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p],
 }

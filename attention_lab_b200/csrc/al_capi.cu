@@ -828,6 +828,84 @@ int al_lse_merge_peer(const float* gather, const unsigned* flags, const unsigned
   return plain_launch_check("lse_merge_wait_kernel");
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ no-allocation entry
+// Scratch of al_context_threshold_noalloc: the ranks' keys gathered into one array on this GPU. It is part of the
+// library image, so every GPU that loads the library holds these 4 MiB until the process exits; no call allocates.
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+static __device__ __align__(256) unsigned long long g_noalloc_keys[kNoAllocScratchBytes / 8];
+
+namespace {
+
+// Device address of g_noalloc_keys on the current device (the host-side symbol is only a stand-in), looked up once per
+// device with that device current.
+unsigned long long* g_noalloc_addr[64];
+
+int noalloc_scratch(unsigned long long** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return fail(AL_ECUDA, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* ptr = nullptr;
+    if ((e = cudaGetSymbolAddress(&ptr, g_noalloc_keys)) != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress");
+    g_noalloc_addr[dev] = static_cast<unsigned long long*>(ptr);
+  }
+  *out = g_noalloc_addr[dev];
+  return AL_OK;
+}
+
+// dst[q * per_rank + i] = src[q][i]: rank q's keys [B, G, key_stride] into slot q of the scratch.
+__global__ void __launch_bounds__(256) gather_rank_keys_kernel(const unsigned long long* const* src, int P,
+                                                                long long per_rank, unsigned long long* dst) {
+  const long long n = (long long)P * per_rank, stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int q = (int)(i / per_rank);
+    dst[i] = src[q][i - (long long)q * per_rank];
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int al_context_threshold_noalloc(const uint64_t* const* rank_keys, int world, int rank, int B, int G, int key_stride,
+                                 int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
+                                 void* stream) {
+  if (!rank_keys || !rows_in || !rows_attend) return fail(AL_EINVAL, "null pointer argument");
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world) return fail(AL_EINVAL, "rank %d outside [0, world=%d)", rank, world);
+  if (B <= 0 || G <= 0 || B * (long long)G > 0x7fffffffLL) return fail(AL_EINVAL, "B and G must be positive");
+  if (k < 1 || key_stride < 1 || k > (long long)world * key_stride)
+    return fail(AL_EINVAL, "k=%d must lie in [1, world*key_stride=%lld]", k, (long long)world * key_stride);
+  if (k_local < 0 || k_local > key_stride || fixed_count < 0)
+    return fail(AL_EINVAL, "k_local=%d must lie in [0, key_stride=%d]", k_local, key_stride);
+  const long long per_rank = (long long)B * G * key_stride;
+  if ((unsigned long long)world * (unsigned long long)per_rank > kNoAllocScratchBytes / 8)
+    return fail(AL_EUNSUPPORTED, "world*B*G*key_stride = %lld keys exceeds the %zu keys of the no-allocation scratch",
+                (long long)world * per_rank, kNoAllocScratchBytes / 8);
+  if (fixed_count + k_local == 0) return AL_OK;
+  DeviceInfo* di = nullptr;
+  int rc = device_info(&di);
+  if (rc) return rc;
+  unsigned long long* scratch = nullptr;
+  if ((rc = noalloc_scratch(&scratch))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const long long n = (long long)world * per_rank;
+  const long long blocks = std::min<long long>((n + 255) / 256, 4LL * di->sms);
+  gather_rank_keys_kernel<<<(unsigned)blocks, 256, 0, st>>>(reinterpret_cast<const unsigned long long* const*>(rank_keys),
+                                                            world, per_rank, scratch);
+  if ((rc = plain_launch_check("gather_rank_keys_kernel"))) return rc;
+  CtxParams p = {};
+  p.P = world; p.B = B; p.G = G; p.kst = key_stride; p.k = k; p.rank = rank; p.F = fixed_count; p.k_local = k_local;
+  p.keys = scratch;
+  p.rows_in = reinterpret_cast<const long long*>(rows_in);
+  p.rows_attend = reinterpret_cast<long long*>(rows_attend);
+  context_threshold_kernel<<<B * G, kThreads, 0, st>>>(p);
+  return plain_launch_check("context_threshold_kernel");
+}
+
 int al_prefill_score_topk(const void* u, long long u_sh, long long u_st, const void* zT, long long z_sh, long long z_ld,
                           int H, int T, int C, int r, int q_pos0, int k, int kcap, int* idx_out, float* scores_out,
                           void* stream) {

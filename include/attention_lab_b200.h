@@ -175,6 +175,19 @@ int al_context_threshold_peer(const uint64_t* gather, const unsigned* flags, con
 int al_lse_merge_peer(const float* gather, const unsigned* flags, const unsigned* counter, int spin, int world,
                       int rank, int B, int G, int h, int d, void* out, int out_dtype, void* stream);
 
+/* n1: al_context_threshold for callers that cannot allocate device memory: a serving runtime that has already handed
+ *   all of the GPU's memory to its own pool, or code that must not call cudaMalloc where it runs (for instance while
+ *   the stream is being captured into a CUDA graph). No counterpart in the reference, and nothing is allocated: rank
+ *   q's keys [B,G,key_stride] are read from rank_keys[q] (device array of world addresses: this GPU's memory or a
+ *   peer's mapped region) into a scratch array that is part of the library image (4 MiB on every GPU that loads the
+ *   library, held until the process exits), and the threshold runs over that copy. world*B*G*key_stride may not
+ *   exceed 524 288 keys (AL_EUNSUPPORTED otherwise). The first call on a device looks up the scratch's device address;
+ *   make it before any stream capture. Every call shares the scratch, so calls that overlap on the GPU (different
+ *   streams, or different host threads) race and must be serialised by the caller. */
+int al_context_threshold_noalloc(const uint64_t* const* rank_keys, int world, int rank, int B, int G, int key_stride,
+                                 int k, int fixed_count, int k_local, const int64_t* rows_in, int64_t* rows_attend,
+                                 void* stream);
+
 /* Batched prefill scorer (config C5). No single reference counterpart: the reference selects nothing during prefill
  * (qwen_wrap.py:287-289); this applies its decode-time selection (candidates of selection.py:71-79 at legal length
  * p + 1, top-k of decode.py:86-93, ties to the smaller position) to every query position p of a prefill chunk.

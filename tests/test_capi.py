@@ -22,7 +22,7 @@ REQUIRED = {"al_sparse_decode_step", "al_select_rows", "al_gathered_attend", "al
             "al_project_keys", "al_project_queries", "al_candidate_scores", "al_context_local_topk",
             "al_context_threshold", "al_gathered_attend_partial", "al_lse_merge", "al_xchg_create", "al_xchg_open",
             "al_xchg_close", "al_xchg_destroy", "al_xchg_push", "al_context_threshold_peer", "al_lse_merge_peer",
-            "al_prefill_score_topk", "al_last_error", "al_version", "al_device_status"}
+            "al_context_threshold_noalloc", "al_prefill_score_topk", "al_last_error", "al_version", "al_device_status"}
 
 
 def test_header_declares_the_bound_entry_points():
